@@ -1,0 +1,514 @@
+// bs_capi.cu -- implementation of the C ABI declared in include/bsearch.h.
+//
+// Index residency in HBM:
+//   vectors   [n][row_stride] f32, row_stride = dim rounded up to 4 (zero pad),
+//             so every row starts on a 16-byte boundary for vector / cp.async loads
+//   adjacency [n][degree] u32, the graph.bin payload unchanged
+//   codes     [n][degree][wpp] u32, factors [n][3][degree] f32, signs [pdim] f32
+//             (RaBitQ, the codebook row layout of include/rabitq.hpp:61-64 with
+//             the raw-vector and neighbour-id slots dropped)
+// Per call: a stream-ordered scratch block (counters, and staging for host
+// buffers) from cudaMallocAsync, released on the same stream.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "../../include/bsearch.h"
+#include "bs_internal.h"
+#include "bs_io.hpp"
+
+using bsb::DevCounters;
+using bsb::LaunchShape;
+using bsb::SearchParams;
+
+struct bs_index {
+    int device = 0;
+    int num_sms = 0;
+    size_t smem_optin = 0;
+    uint64_t n = 0;
+    int32_t dim = 0;
+    int32_t degree = 0;
+    uint32_t row_stride = 0;
+    float* d_vecs = nullptr;
+    uint32_t* d_adj = nullptr;
+    bool int_exact = false;
+    float max_abs = 0.0f;
+    // RaBitQ
+    bool has_rabitq = false;
+    uint32_t rq_entry = BS_NO_NODE;
+    int32_t pdim = 0;
+    uint32_t* d_codes = nullptr;
+    float* d_factors = nullptr;
+    float* d_signs = nullptr;
+    // cached centroid-nearest entry
+    std::mutex mu;
+    bool entry_valid = false;
+    uint32_t entry = 0;
+};
+
+namespace {
+
+thread_local std::string g_err;
+
+bs_status fail(bs_status s, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    std::vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_err = buf;
+    return s;
+}
+
+bs_status cuda_fail(cudaError_t e, const char* what) {
+    if (e == cudaErrorMemoryAllocation)
+        return fail(BS_ERR_OUT_OF_MEMORY, "%s: %s", what, cudaGetErrorString(e));
+    return fail(BS_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+// Makes the index's device current for the scope and restores the caller's.
+struct DeviceGuard {
+    int prev = -1;
+    bool ok = false;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        ok = cudaSetDevice(dev) == cudaSuccess;
+    }
+    ~DeviceGuard() {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
+
+// true: device (or managed) memory usable by kernels on `device`.
+bool is_device_ptr(const void* ptr) {
+    if (!ptr) return false;
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, ptr) != cudaSuccess) {
+        cudaGetLastError();   // clear the sticky-free error of an unknown pointer
+        return false;
+    }
+    return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+}
+
+struct ModeInfo {
+    bool rabitq = false;
+    bsb::FilterMode fmode = bsb::kHash;
+    int warps = 4;
+};
+
+bool parse_mode(const char* m, ModeInfo& mi) {
+    if (!m) return false;
+    const std::string s(m);
+    if (s == "base") { mi = {false, bsb::kHash, 4}; return true; }
+    if (s == "rabitq") { mi = {true, bsb::kHash, 4}; return true; }
+    const struct { const char* name; bsb::FilterMode f; int w; } table[] = {
+        {"warp1", bsb::kHash, 1},   {"warp2", bsb::kHash, 2},   {"warp4", bsb::kHash, 4},
+        {"warp8", bsb::kHash, 8},   {"bwarp1", bsb::kBloom, 1}, {"bwarp2", bsb::kBloom, 2},
+        {"bwarp4", bsb::kBloom, 4}, {"bwarp8", bsb::kBloom, 8},
+    };
+    for (const auto& t : table)
+        if (s == t.name) { mi = {false, t.f, t.w}; return true; }
+    return false;
+}
+
+// Largest |value| and whether every value is an integer (multi-threaded scan
+// of the host array at index creation).
+void scan_values(const float* v, uint64_t count, bool& all_int, float& max_abs) {
+    unsigned nt = std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
+    if (count < (1u << 20)) nt = 1;
+    std::vector<char> ints(nt, 1);
+    std::vector<float> maxes(nt, 0.0f);
+    std::vector<std::thread> th;
+    const uint64_t per = (count + nt - 1) / nt;
+    for (unsigned t = 0; t < nt; ++t) {
+        th.emplace_back([&, t] {
+            const uint64_t lo = per * t, hi = std::min(count, lo + per);
+            bool ok = true;
+            float mx = 0.0f;
+            for (uint64_t i = lo; i < hi; ++i) {
+                const float x = v[i];
+                ok = ok && (x == std::nearbyint(x));
+                const float a = std::fabs(x);
+                mx = a > mx ? a : mx;
+                if (!(a == a)) ok = false;
+            }
+            ints[t] = ok;
+            maxes[t] = mx;
+        });
+    }
+    for (auto& t : th) t.join();
+    all_int = true;
+    max_abs = 0.0f;
+    for (unsigned t = 0; t < nt; ++t) {
+        all_int = all_int && ints[t];
+        max_abs = std::max(max_abs, maxes[t]);
+    }
+}
+
+// |q| bound that keeps dim * (|q| + |x|max)^2 <= 2^24 (all partial sums exact).
+float team_qmax_for(const bs_index* ix) {
+    if (!ix->int_exact) return -1.0f;
+    const double lim = std::floor(std::sqrt(16777216.0 / ix->dim) - ix->max_abs);
+    return lim >= 0.0 ? static_cast<float>(lim) : -1.0f;
+}
+
+bool force_seq() {
+    const char* e = std::getenv("BSEARCH_FORCE_SEQ");
+    return e && e[0] && e[0] != '0';
+}
+
+void free_index(bs_index* ix) {
+    if (!ix) return;
+    DeviceGuard g(ix->device);
+    cudaFree(ix->d_vecs);
+    cudaFree(ix->d_adj);
+    cudaFree(ix->d_codes);
+    cudaFree(ix->d_factors);
+    cudaFree(ix->d_signs);
+    delete ix;
+}
+
+bs_status ensure_entry(bs_index* ix) {
+    std::lock_guard<std::mutex> lk(ix->mu);
+    if (ix->entry_valid) return BS_OK;
+    const size_t bytes = bsb::entry_point_scratch_bytes(ix->n, ix->dim) + 8;
+    void* scratch = nullptr;
+    cudaError_t e = cudaMalloc(&scratch, bytes);
+    if (e != cudaSuccess) return cuda_fail(e, "entry point scratch");
+    uint32_t* d_out = reinterpret_cast<uint32_t*>(static_cast<char*>(scratch) + bytes - 8);
+    e = bsb::compute_entry_point(ix->d_vecs, ix->n, ix->dim, ix->row_stride, d_out,
+                                 static_cast<float*>(scratch), nullptr);
+    uint32_t h = 0;
+    if (e == cudaSuccess) e = cudaMemcpy(&h, d_out, 4, cudaMemcpyDeviceToHost);
+    cudaFree(scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "entry point kernel");
+    ix->entry = h;
+    ix->entry_valid = true;
+    return BS_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+BS_API void bs_search_params_default(bs_search_params* p) {
+    if (!p) return;
+    p->mode = "base";
+    p->K = 100;
+    p->topk_size = 256;
+    p->filter_capacity = 1024;
+    p->max_iterations = 1024;
+    p->reset_interval = 16;
+    p->entry_point = BS_NO_NODE;
+}
+
+BS_API const char* bs_last_error(void) { return g_err.c_str(); }
+
+BS_API const char* bs_version(void) { return "beam_search_collab_b200 0.1 (sm_100a)"; }
+
+BS_API bs_status bs_index_create(const bs_graph_desc* desc, int device, bs_index** out) {
+    if (!out) return fail(BS_ERR_INVALID_ARGUMENT, "out is NULL");
+    *out = nullptr;
+    if (!desc || !desc->vectors || !desc->edges) return fail(BS_ERR_INVALID_ARGUMENT, "graph descriptor or its arrays are NULL");
+    if (desc->num_nodes == 0 || desc->dim <= 0 || desc->degree <= 0)
+        return fail(BS_ERR_INVALID_ARGUMENT, "num_nodes, dim and degree must be positive");
+    if (desc->num_nodes >= (1ull << 31))
+        return fail(BS_ERR_UNSUPPORTED, "num_nodes must be below 2^31 (node ids are 31-bit)");
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
+        cudaGetLastError();
+        return fail(BS_ERR_CUDA, "no CUDA device available");
+    }
+    if (device < 0 || device >= ndev) return fail(BS_ERR_INVALID_ARGUMENT, "device %d out of range", device);
+
+    DeviceGuard g(device);
+    if (!g.ok) return fail(BS_ERR_CUDA, "cannot select device %d", device);
+    auto* ix = new (std::nothrow) bs_index();
+    if (!ix) return fail(BS_ERR_OUT_OF_MEMORY, "host allocation failed");
+    ix->device = device;
+    ix->n = desc->num_nodes;
+    ix->dim = desc->dim;
+    ix->degree = desc->degree;
+    ix->row_stride = (static_cast<uint32_t>(desc->dim) + 3u) & ~3u;
+    cudaDeviceProp prop;
+    cudaError_t e = cudaGetDeviceProperties(&prop, device);
+    if (e != cudaSuccess) { free_index(ix); return cuda_fail(e, "cudaGetDeviceProperties"); }
+    ix->num_sms = prop.multiProcessorCount;
+    ix->smem_optin = prop.sharedMemPerBlockOptin;
+
+    const size_t vbytes = static_cast<size_t>(ix->n) * ix->row_stride * sizeof(float);
+    const size_t ebytes = static_cast<size_t>(ix->n) * ix->degree * sizeof(uint32_t);
+    if ((e = cudaMalloc(&ix->d_vecs, vbytes)) != cudaSuccess) { free_index(ix); return cuda_fail(e, "vectors"); }
+    if ((e = cudaMalloc(&ix->d_adj, ebytes)) != cudaSuccess) { free_index(ix); return cuda_fail(e, "adjacency"); }
+    if (ix->row_stride == static_cast<uint32_t>(ix->dim)) {
+        e = cudaMemcpy(ix->d_vecs, desc->vectors, vbytes, cudaMemcpyHostToDevice);
+    } else {
+        e = cudaMemset(ix->d_vecs, 0, vbytes);
+        if (e == cudaSuccess)
+            e = cudaMemcpy2D(ix->d_vecs, ix->row_stride * sizeof(float), desc->vectors,
+                             ix->dim * sizeof(float), ix->dim * sizeof(float), ix->n,
+                             cudaMemcpyHostToDevice);
+    }
+    if (e == cudaSuccess) e = cudaMemcpy(ix->d_adj, desc->edges, ebytes, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) { free_index(ix); return cuda_fail(e, "index upload"); }
+    scan_values(desc->vectors, static_cast<uint64_t>(ix->n) * ix->dim, ix->int_exact, ix->max_abs);
+    *out = ix;
+    return BS_OK;
+}
+
+BS_API bs_status bs_index_load(const char* graph_bin, const char* base_fvecs, int device, bs_index** out) {
+    if (!graph_bin || !base_fvecs) return fail(BS_ERR_INVALID_ARGUMENT, "file path is NULL");
+    uint64_t n = 0, nv = 0;
+    int32_t deg = 0, dim = 0;
+    std::vector<uint32_t> edges;
+    std::vector<float> vecs;
+    std::string err;
+    if (!bsb::io::read_graph(graph_bin, n, deg, edges, err)) return fail(BS_ERR_IO, "%s", err.c_str());
+    if (!bsb::io::read_vecs<float>(base_fvecs, nv, dim, vecs, err)) return fail(BS_ERR_IO, "%s", err.c_str());
+    if (nv != n)
+        return fail(BS_ERR_IO, "graph has %llu nodes but %s has %llu vectors", static_cast<unsigned long long>(n),
+                    base_fvecs, static_cast<unsigned long long>(nv));
+    bs_graph_desc d{n, dim, deg, vecs.data(), edges.data()};
+    return bs_index_create(&d, device, out);
+}
+
+BS_API bs_status bs_index_attach_rabitq(bs_index* ix, const bs_rabitq_desc* d) {
+    if (!ix || !d || !d->codes || !d->factors || !d->signs)
+        return fail(BS_ERR_INVALID_ARGUMENT, "index or RaBitQ arrays are NULL");
+    const int32_t pdim = bsb::io::padded_dim_of(ix->dim);
+    if (d->padded_dim != pdim)
+        return fail(BS_ERR_INVALID_ARGUMENT, "padded_dim %d does not match dim %d (expected %d)", d->padded_dim,
+                    ix->dim, pdim);
+    if (pdim < 32) return fail(BS_ERR_UNSUPPORTED, "RaBitQ needs dim > 16 (padded_dim >= 32)");
+    if (d->entry_point != BS_NO_NODE && d->entry_point >= ix->n)
+        return fail(BS_ERR_INVALID_ARGUMENT, "codebook entry point %u out of range", d->entry_point);
+    DeviceGuard g(ix->device);
+    const size_t wpp = static_cast<size_t>(pdim) / 32;
+    const size_t cbytes = static_cast<size_t>(ix->n) * ix->degree * wpp * 4;
+    const size_t fbytes = static_cast<size_t>(ix->n) * 3 * ix->degree * 4;
+    cudaFree(ix->d_codes);
+    cudaFree(ix->d_factors);
+    cudaFree(ix->d_signs);
+    ix->d_codes = nullptr; ix->d_factors = nullptr; ix->d_signs = nullptr;
+    ix->has_rabitq = false;
+    cudaError_t e;
+    if ((e = cudaMalloc(&ix->d_codes, cbytes)) != cudaSuccess) return cuda_fail(e, "codes");
+    if ((e = cudaMalloc(&ix->d_factors, fbytes)) != cudaSuccess) return cuda_fail(e, "factors");
+    if ((e = cudaMalloc(&ix->d_signs, pdim * 4)) != cudaSuccess) return cuda_fail(e, "signs");
+    if ((e = cudaMemcpy(ix->d_codes, d->codes, cbytes, cudaMemcpyHostToDevice)) != cudaSuccess ||
+        (e = cudaMemcpy(ix->d_factors, d->factors, fbytes, cudaMemcpyHostToDevice)) != cudaSuccess ||
+        (e = cudaMemcpy(ix->d_signs, d->signs, pdim * 4, cudaMemcpyHostToDevice)) != cudaSuccess)
+        return cuda_fail(e, "codebook upload");
+    ix->pdim = pdim;
+    ix->rq_entry = d->entry_point;
+    ix->has_rabitq = true;
+    return BS_OK;
+}
+
+BS_API bs_status bs_index_load_codebook(bs_index* ix, const char* path) {
+    if (!ix || !path) return fail(BS_ERR_INVALID_ARGUMENT, "index or path is NULL");
+    bsb::io::Codebook cb;
+    std::string err;
+    if (!bsb::io::read_codebook(path, ix->n, ix->dim, ix->degree, cb, err)) return fail(BS_ERR_IO, "%s", err.c_str());
+    bs_rabitq_desc d{cb.entry, cb.padded_dim, cb.codes.data(), cb.factors.data(), cb.signs.data()};
+    return bs_index_attach_rabitq(ix, &d);
+}
+
+BS_API bs_status bs_index_info(const bs_index* ix, uint64_t* n, int32_t* dim, int32_t* degree) {
+    if (!ix) return fail(BS_ERR_INVALID_ARGUMENT, "index is NULL");
+    if (n) *n = ix->n;
+    if (dim) *dim = ix->dim;
+    if (degree) *degree = ix->degree;
+    return BS_OK;
+}
+
+BS_API bs_status bs_index_entry_point(bs_index* ix, uint32_t* entry) {
+    if (!ix || !entry) return fail(BS_ERR_INVALID_ARGUMENT, "index or entry is NULL");
+    DeviceGuard g(ix->device);
+    const bs_status s = ensure_entry(ix);
+    if (s != BS_OK) return s;
+    *entry = ix->entry;
+    return BS_OK;
+}
+
+BS_API bs_status bs_index_rabitq_entry(const bs_index* ix, uint32_t* entry) {
+    if (!ix || !entry) return fail(BS_ERR_INVALID_ARGUMENT, "index or entry is NULL");
+    *entry = ix->has_rabitq ? ix->rq_entry : BS_NO_NODE;
+    return BS_OK;
+}
+
+BS_API void bs_index_destroy(bs_index* ix) { free_index(ix); }
+
+BS_API bs_status bs_search(bs_index* ix, const bs_search_params* prm, const float* queries, uint32_t nq,
+                           uint32_t* ids, float* dists, bs_stats* stats, void* stream_) {
+    if (!ix || !prm) return fail(BS_ERR_INVALID_ARGUMENT, "index or params is NULL");
+    ModeInfo mi;
+    if (!parse_mode(prm->mode, mi)) return fail(BS_ERR_INVALID_ARGUMENT, "Unknown mode: %s", prm->mode ? prm->mode : "(null)");
+    if (prm->K <= 0) return fail(BS_ERR_INVALID_ARGUMENT, "K must be positive");
+    if (prm->topk_size == 0) return fail(BS_ERR_INVALID_ARGUMENT, "topk_size must be positive");
+    if (prm->max_iterations < 0) return fail(BS_ERR_INVALID_ARGUMENT, "max_iterations must be >= 0");
+    if (mi.rabitq && !ix->has_rabitq) return fail(BS_ERR_INVALID_ARGUMENT, "rabitq mode requires a codebook on the index");
+    if (nq > 0 && (!queries || !ids)) return fail(BS_ERR_INVALID_ARGUMENT, "queries or ids is NULL");
+
+    DeviceGuard g(ix->device);
+    if (!g.ok) return fail(BS_ERR_CUDA, "cannot select device %d", ix->device);
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+
+    uint32_t entry = prm->entry_point;
+    if (entry == BS_NO_NODE) {
+        if (mi.rabitq && ix->rq_entry != BS_NO_NODE) {
+            entry = ix->rq_entry;
+        } else {
+            const bs_status s = ensure_entry(ix);
+            if (s != BS_OK) return s;
+            entry = ix->entry;
+        }
+    }
+    if (entry >= ix->n) return fail(BS_ERR_INVALID_ARGUMENT, "entry point %u out of range", entry);
+
+    SearchParams p{};
+    p.vecs = ix->d_vecs;
+    p.adj = ix->d_adj;
+    p.n = ix->n;
+    p.dim = static_cast<uint32_t>(ix->dim);
+    p.row_stride = ix->row_stride;
+    p.degree = static_cast<uint32_t>(ix->degree);
+    if (mi.rabitq) {
+        p.codes = ix->d_codes;
+        p.factors = ix->d_factors;
+        p.signs = ix->d_signs;
+        p.pdim = static_cast<uint32_t>(ix->pdim);
+        p.wpp = static_cast<uint32_t>(ix->pdim) / 32u;
+    }
+    p.nq = nq;
+    p.topk = prm->topk_size;
+    p.K = static_cast<uint32_t>(prm->K);
+    p.entry = entry;
+    p.max_iterations = prm->max_iterations;
+    p.filter_slots = prm->filter_capacity;
+    p.reset_interval = prm->reset_interval;
+    const bool use_team = !force_seq() && ix->int_exact && team_qmax_for(ix) >= 0.0f;
+    p.team_qmax = use_team ? team_qmax_for(ix) : -1.0f;
+
+    LaunchShape shape{};
+    shape.dmode = use_team ? bsb::kTeam : bsb::kSeq;
+    shape.fmode = mi.fmode;
+    shape.warps_per_block = mi.warps;
+    char why[256] = {0};
+    if (bsb::plan_search(p, shape, ix->smem_optin, why, sizeof(why)) != cudaSuccess)
+        return fail(BS_ERR_UNSUPPORTED, "%s", why);
+
+    if (stats) {
+        std::memset(stats, 0, sizeof(*stats));
+        stats->entry_point = entry;
+        stats->integer_exact = use_team ? 1u : 0u;
+    }
+    if (nq == 0) return BS_OK;
+
+    const bool q_dev = is_device_ptr(queries);
+    const bool i_dev = is_device_ptr(ids);
+    const bool d_dev = dists ? is_device_ptr(dists) : true;
+    const size_t qbytes = static_cast<size_t>(nq) * ix->dim * sizeof(float);
+    const size_t obytes = static_cast<size_t>(nq) * p.K * sizeof(uint32_t);
+    size_t off = 256;   // DevCounters at 0
+    const size_t q_off = off;
+    if (!q_dev) off += (qbytes + 255) & ~static_cast<size_t>(255);
+    const size_t i_off = off;
+    if (!i_dev) off += (obytes + 255) & ~static_cast<size_t>(255);
+    const size_t d_off = off;
+    if (dists && !d_dev) off += (obytes + 255) & ~static_cast<size_t>(255);
+
+    char* scratch = nullptr;
+    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&scratch), off, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "search scratch");
+    auto release = [&]() { cudaFreeAsync(scratch, stream); };
+    p.counters = reinterpret_cast<DevCounters*>(scratch);
+    p.queries = q_dev ? queries : reinterpret_cast<const float*>(scratch + q_off);
+    p.out_ids = i_dev ? ids : reinterpret_cast<uint32_t*>(scratch + i_off);
+    p.out_dists = dists ? (d_dev ? dists : reinterpret_cast<float*>(scratch + d_off)) : nullptr;
+
+    e = cudaMemsetAsync(scratch, 0, sizeof(DevCounters), stream);
+    if (e == cudaSuccess && !q_dev)
+        e = cudaMemcpyAsync(scratch + q_off, queries, qbytes, cudaMemcpyHostToDevice, stream);
+    if (e != cudaSuccess) { release(); return cuda_fail(e, "query upload"); }
+
+    e = mi.rabitq ? bsb::launch_search_rabitq(p, shape, ix->num_sms, stream)
+                  : bsb::launch_search(p, shape, ix->num_sms, stream);
+    if (e != cudaSuccess) { release(); return cuda_fail(e, "search launch"); }
+
+    if (!i_dev) e = cudaMemcpyAsync(ids, scratch + i_off, obytes, cudaMemcpyDeviceToHost, stream);
+    if (e == cudaSuccess && dists && !d_dev)
+        e = cudaMemcpyAsync(dists, scratch + d_off, obytes, cudaMemcpyDeviceToHost, stream);
+    DevCounters hc{};
+    const bool sync = stats || !q_dev || !i_dev || !d_dev;
+    if (e == cudaSuccess && sync)
+        e = cudaMemcpyAsync(&hc, scratch, sizeof(hc), cudaMemcpyDeviceToHost, stream);
+    release();
+    if (e != cudaSuccess) return cuda_fail(e, "result download");
+    if (!sync) return BS_OK;
+    e = cudaStreamSynchronize(stream);
+    if (e != cudaSuccess) return cuda_fail(e, "search");
+    if (stats) {
+        stats->expansions = hc.expansions;
+        stats->distances = hc.distances;
+        stats->estimates = hc.estimates;
+        stats->rerank = hc.rerank;
+        stats->error_flags = hc.error_flags;
+        stats->integer_exact = (use_team && hc.team_fallbacks == 0) ? 1u : 0u;
+    }
+    if (hc.error_flags) return fail(BS_ERR_KERNEL, "search kernel reported error flags 0x%x", hc.error_flags);
+    return BS_OK;
+}
+
+BS_API bs_status bs_device_alloc(const bs_index* ix, size_t bytes, void** dptr) {
+    if (!ix || !dptr) return fail(BS_ERR_INVALID_ARGUMENT, "index or dptr is NULL");
+    DeviceGuard g(ix->device);
+    const cudaError_t e = cudaMalloc(dptr, bytes ? bytes : 1);
+    return e == cudaSuccess ? BS_OK : cuda_fail(e, "bs_device_alloc");
+}
+
+BS_API bs_status bs_device_free(const bs_index* ix, void* dptr) {
+    if (!ix) return fail(BS_ERR_INVALID_ARGUMENT, "index is NULL");
+    DeviceGuard g(ix->device);
+    const cudaError_t e = cudaFree(dptr);
+    return e == cudaSuccess ? BS_OK : cuda_fail(e, "bs_device_free");
+}
+
+BS_API bs_status bs_copy_to_device(const bs_index* ix, void* dst, const void* src, size_t bytes) {
+    if (!ix) return fail(BS_ERR_INVALID_ARGUMENT, "index is NULL");
+    DeviceGuard g(ix->device);
+    const cudaError_t e = cudaMemcpy(dst, src, bytes, cudaMemcpyHostToDevice);
+    return e == cudaSuccess ? BS_OK : cuda_fail(e, "bs_copy_to_device");
+}
+
+BS_API bs_status bs_copy_to_host(const bs_index* ix, void* dst, const void* src, size_t bytes) {
+    if (!ix) return fail(BS_ERR_INVALID_ARGUMENT, "index is NULL");
+    DeviceGuard g(ix->device);
+    const cudaError_t e = cudaMemcpy(dst, src, bytes, cudaMemcpyDeviceToHost);
+    return e == cudaSuccess ? BS_OK : cuda_fail(e, "bs_copy_to_host");
+}
+
+BS_API bs_status bs_device_fill(const bs_index* ix, void* dptr, int byte_value, size_t bytes) {
+    if (!ix) return fail(BS_ERR_INVALID_ARGUMENT, "index is NULL");
+    DeviceGuard g(ix->device);
+    const cudaError_t e = cudaMemset(dptr, byte_value, bytes);
+    return e == cudaSuccess ? BS_OK : cuda_fail(e, "bs_device_fill");
+}
+
+BS_API bs_status bs_synchronize(const bs_index* ix, void* stream) {
+    if (!ix) return fail(BS_ERR_INVALID_ARGUMENT, "index is NULL");
+    DeviceGuard g(ix->device);
+    const cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? BS_OK : cuda_fail(e, "bs_synchronize");
+}
+
+}  // extern "C"

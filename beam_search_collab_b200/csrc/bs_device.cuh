@@ -1,0 +1,262 @@
+// bs_device.cuh -- warp-level device primitives of the beam search.
+//
+//  * 64-bit beam keys: (order-preserving fp32 distance, node id, expanded bit)
+//    so that every comparison is the reference CPU comparator "(dist, id)"
+//    (include/cpu_search_base.hpp:48-51) in one integer compare.
+//  * register-resident bitonic sort / merge over a striped warp layout
+//    (element p lives in register p/32 of lane p%32); the beam's role is that
+//    of RegBitonicTopK (include/topk_reg.cuh) but ordered by (dist, id).
+//  * shared-memory visited filters (exact hash set, Bloom filter).
+//  * the two distance evaluators (sequential per lane, or 8-lane teams).
+#pragma once
+
+#include <cfloat>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace bsb {
+namespace dev {
+
+constexpr unsigned kFull = 0xffffffffu;
+constexpr uint64_t kEmptyKey = ~0ull;
+constexpr uint32_t kNoNode = 0xffffffffu;
+
+// ---------------------------------------------------------------- beam keys
+
+// Monotone map fp32 -> u32 (negative values flip all bits, others set the
+// sign bit).  -0 is folded onto +0 because the reference comparator treats
+// them as equal.
+__device__ __forceinline__ uint32_t f2ord(float f) {
+    uint32_t u = __float_as_uint(f);
+    if (u == 0x80000000u) u = 0u;
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+__device__ __forceinline__ float ord2f(uint32_t o) {
+    const uint32_t u = (o & 0x80000000u) ? (o & 0x7fffffffu) : ~o;
+    return __uint_as_float(u);
+}
+
+// key = ord(dist) << 32 | id << 1 | expanded.  Node ids are < 2^31, ids are
+// unique inside a beam, so the expanded bit never decides an order.
+__device__ __forceinline__ uint64_t make_key(float d, uint32_t id) {
+    return (static_cast<uint64_t>(f2ord(d)) << 32) | (static_cast<uint64_t>(id) << 1);
+}
+__device__ __forceinline__ uint32_t key_id(uint64_t k) { return static_cast<uint32_t>(k) >> 1; }
+__device__ __forceinline__ float key_dist(uint64_t k) { return ord2f(static_cast<uint32_t>(k >> 32)); }
+__device__ __forceinline__ uint64_t kmin(uint64_t a, uint64_t b) { return a < b ? a : b; }
+__device__ __forceinline__ uint64_t kmax(uint64_t a, uint64_t b) { return a < b ? b : a; }
+
+// ------------------------------------------------------- bitonic networks
+
+// One compare-exchange stage of a bitonic network of 32*N elements in the
+// striped layout.  SIZE is the bitonic block size (direction ascending when
+// (p & SIZE) == 0), STRIDE the partner distance.  Both are template constants
+// so the whole network unrolls into register moves and shuffles.
+template <int N, unsigned SIZE, unsigned STRIDE>
+__device__ __forceinline__ void cmpx_stage(uint64_t (&k)[N], unsigned lane) {
+    if constexpr (STRIDE >= 32) {
+        constexpr unsigned rs = STRIDE >> 5;
+#pragma unroll
+        for (int r = 0; r < N; ++r) {
+            if ((static_cast<unsigned>(r) & rs) == 0) {
+                const int r2 = r | static_cast<int>(rs);
+                const bool asc = ((static_cast<unsigned>(r) * 32u) & SIZE) == 0;
+                const uint64_t lo = kmin(k[r], k[r2]);
+                const uint64_t hi = kmax(k[r], k[r2]);
+                k[r] = asc ? lo : hi;
+                k[r2] = asc ? hi : lo;
+            }
+        }
+    } else {
+        const bool lower = (lane & STRIDE) == 0;
+#pragma unroll
+        for (int r = 0; r < N; ++r) {
+            const uint64_t o = __shfl_xor_sync(kFull, k[r], STRIDE);
+            const unsigned p = static_cast<unsigned>(r) * 32u + lane;
+            const bool asc = (p & SIZE) == 0;
+            k[r] = (asc == lower) ? kmin(k[r], o) : kmax(k[r], o);
+        }
+    }
+}
+
+template <int N, unsigned SIZE, unsigned STRIDE>
+__device__ __forceinline__ void merge_stages(uint64_t (&k)[N], unsigned lane) {
+    if constexpr (STRIDE > 0) {
+        cmpx_stage<N, SIZE, STRIDE>(k, lane);
+        merge_stages<N, SIZE, STRIDE / 2>(k, lane);
+    }
+}
+
+template <int N, unsigned SIZE>
+__device__ __forceinline__ void sort_stages(uint64_t (&k)[N], unsigned lane) {
+    if constexpr (SIZE >= 2) {
+        sort_stages<N, SIZE / 2>(k, lane);
+        merge_stages<N, SIZE, SIZE / 2>(k, lane);
+    }
+}
+
+// Full ascending sort of 32*N keys.
+template <int N>
+__device__ __forceinline__ void sort_asc(uint64_t (&k)[N], unsigned lane) {
+    sort_stages<N, 32u * N>(k, lane);
+}
+
+// Bitonic 32*N keys -> ascending (one merge pass).
+template <int N>
+__device__ __forceinline__ void merge_asc(uint64_t (&k)[N], unsigned lane) {
+    merge_stages<N, 32u * N, 16u * N>(k, lane);
+}
+
+// Keep the `topk` smallest keys of beam (ascending, 32*RX) and cand (any
+// order, 32*RY), ascending in beam.  cand is clobbered.
+template <int RX, int RY>
+__device__ __forceinline__ void beam_merge(uint64_t (&beam)[RX], uint64_t (&cand)[RY],
+                                           unsigned lane, unsigned topk) {
+    static_assert(RX >= RY, "beam must be at least as wide as the candidate batch");
+    sort_asc<RY>(cand, lane);
+    // Pair the beam's largest 32*RY positions with the candidates reversed:
+    // min() of an ascending and a descending run keeps the smallest half and
+    // leaves a bitonic sequence.
+#pragma unroll
+    for (int r = RX - RY; r < RX; ++r) {
+        const uint64_t c = __shfl_xor_sync(kFull, cand[RX - 1 - r], 31);
+        beam[r] = kmin(beam[r], c);
+    }
+    merge_asc<RX>(beam, lane);
+#pragma unroll
+    for (int r = 0; r < RX; ++r)
+        if (static_cast<unsigned>(r) * 32u + lane >= topk) beam[r] = kEmptyKey;
+}
+
+// Smallest unexpanded entry: mark it and return its node id.  Branch-free
+// over the registers so the beam stays in registers.
+template <int RX>
+__device__ __forceinline__ bool beam_pick(uint64_t (&beam)[RX], unsigned lane, uint32_t& node) {
+    int sel = -1;
+    unsigned sel_mask = 0;
+#pragma unroll
+    for (int r = 0; r < RX; ++r) {
+        const bool open = beam[r] != kEmptyKey && (beam[r] & 1ull) == 0;
+        const unsigned m = __ballot_sync(kFull, open);
+        if (sel < 0 && m != 0) { sel = r; sel_mask = m; }
+    }
+    if (sel < 0) return false;
+    const int src = __ffs(sel_mask) - 1;
+    uint32_t mine = 0;
+#pragma unroll
+    for (int r = 0; r < RX; ++r)
+        if (r == sel) mine = static_cast<uint32_t>(beam[r]) >> 1;
+    node = __shfl_sync(kFull, mine, src);
+    if (static_cast<int>(lane) == src) {
+#pragma unroll
+        for (int r = 0; r < RX; ++r)
+            if (r == sel) beam[r] |= 1ull;
+    }
+    return true;
+}
+
+// ------------------------------------------------------------ filters
+
+// Exact visited set: linear probing on a power-of-two table of node ids
+// (0xffffffff = empty).  Returns 1 when the key was inserted, 0 when it was
+// already present.
+__device__ __forceinline__ uint32_t hash_slot(uint32_t key, uint32_t shift) {
+    return (key * 0x9E3779B1u) >> shift;
+}
+
+__device__ __forceinline__ int hash_insert(uint32_t* tab, uint32_t mask, uint32_t shift,
+                                           uint32_t key, unsigned& err) {
+    uint32_t h = hash_slot(key, shift);
+    for (uint32_t i = 0; i <= mask; ++i) {
+        const uint32_t old = atomicCAS(&tab[h], kNoNode, key);
+        if (old == kNoNode) return 1;
+        if (old == key) return 0;
+        h = (h + 1) & mask;
+    }
+    err |= 1u;   // table full: cannot happen with the host's load bound
+    return 1;
+}
+
+// Bloom filter with the three hashes of include/filter_bloom.cuh:25-38.
+__device__ __forceinline__ void bloom_hashes(uint32_t key, uint32_t mask, uint32_t (&h)[3]) {
+    uint32_t a = key;
+    a ^= a >> 16; a *= 0x45d9f3bu; a ^= a >> 16;
+    uint32_t b = key * 0x9e3779b9u;
+    b ^= b >> 16; b *= 0x45d9f3bu; b ^= b >> 16;
+    uint32_t c = key * 0x517cc1b7u;
+    c ^= c >> 16; c *= 0x45d9f3bu; c ^= c >> 16;
+    h[0] = a & mask; h[1] = b & mask; h[2] = c & mask;
+}
+
+__device__ __forceinline__ bool bloom_test(const uint32_t* w, uint32_t mask, uint32_t key) {
+    uint32_t h[3];
+    bloom_hashes(key, mask, h);
+    return ((w[h[0] >> 5] >> (h[0] & 31)) & (w[h[1] >> 5] >> (h[1] & 31)) &
+            (w[h[2] >> 5] >> (h[2] & 31)) & 1u) != 0;
+}
+
+__device__ __forceinline__ void bloom_set(uint32_t* w, uint32_t mask, uint32_t key) {
+    uint32_t h[3];
+    bloom_hashes(key, mask, h);
+    atomicOr(&w[h[0] >> 5], 1u << (h[0] & 31));
+    atomicOr(&w[h[1] >> 5], 1u << (h[1] & 31));
+    atomicOr(&w[h[2] >> 5], 1u << (h[2] & 31));
+}
+
+// ------------------------------------------------------------ memory ops
+
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+    const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem_dst));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem_src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;\n" ::: "memory");
+}
+
+__device__ __forceinline__ float4 ldg_stream4(const float* p) {
+    float4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];\n"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ uint32_t ldg_u32(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.global.nc.u32 %0, [%1];\n" : "=r"(v) : "l"(p));
+    return v;
+}
+
+// ------------------------------------------------------------ distances
+
+// Reference order (include/cpu_search_base.hpp:29-37): sum += diff*diff for
+// d = 0..dim-1, every operation rounded on its own (no FMA contraction).
+__device__ __forceinline__ float l2_seq(const float* __restrict__ q, const float* __restrict__ x,
+                                        uint32_t dim) {
+    float s = 0.0f;
+    uint32_t d = 0;
+    for (; d + 8 <= dim; d += 8) {
+        const float4 a0 = *reinterpret_cast<const float4*>(q + d);
+        const float4 b0 = *reinterpret_cast<const float4*>(x + d);
+        const float4 a1 = *reinterpret_cast<const float4*>(q + d + 4);
+        const float4 b1 = *reinterpret_cast<const float4*>(x + d + 4);
+        float t;
+        t = __fsub_rn(a0.x, b0.x); s = __fadd_rn(s, __fmul_rn(t, t));
+        t = __fsub_rn(a0.y, b0.y); s = __fadd_rn(s, __fmul_rn(t, t));
+        t = __fsub_rn(a0.z, b0.z); s = __fadd_rn(s, __fmul_rn(t, t));
+        t = __fsub_rn(a0.w, b0.w); s = __fadd_rn(s, __fmul_rn(t, t));
+        t = __fsub_rn(a1.x, b1.x); s = __fadd_rn(s, __fmul_rn(t, t));
+        t = __fsub_rn(a1.y, b1.y); s = __fadd_rn(s, __fmul_rn(t, t));
+        t = __fsub_rn(a1.z, b1.z); s = __fadd_rn(s, __fmul_rn(t, t));
+        t = __fsub_rn(a1.w, b1.w); s = __fadd_rn(s, __fmul_rn(t, t));
+    }
+    for (; d < dim; ++d) {
+        const float t = __fsub_rn(q[d], x[d]);
+        s = __fadd_rn(s, __fmul_rn(t, t));
+    }
+    return s;
+}
+
+}  // namespace dev
+}  // namespace bsb

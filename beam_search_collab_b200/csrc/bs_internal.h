@@ -1,0 +1,121 @@
+// bs_internal.h -- launch-level structures shared by the C ABI (bs_capi.cu)
+// and the search kernels (bs_search.cu).  Not part of the public ABI.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace bsb {
+
+// Distance evaluation order.
+//   kSeq : one lane per candidate row, fp32 sum over d = 0..dim-1 with each
+//          multiply and add rounded separately -- the order of the reference
+//          CPU search (include/cpu_search_base.hpp:29-37), so distances are
+//          bit-identical to cpu_cli for any data.
+//   kTeam: eight lanes per row, coalesced 16-byte loads and a shuffle tree.
+//          Chosen only when every base and query value is an integer small
+//          enough that all partial sums are exact in fp32, in which case any
+//          order gives the same bits.
+enum DistMode : int { kSeq = 0, kTeam = 1 };
+
+// Visited filter.
+//   kHash : exact set in shared memory; cleared and refilled from the beam when
+//           its load would pass a bound.  Never drops an unvisited node, so
+//           results equal the reference cpu_cli (warpN and base modes).
+//   kBloom: Bloom filter with the reference's three hashes
+//           (include/filter_bloom.cuh:25-38), reset every reset_interval
+//           expansions (bwarpN modes).  False positives skip nodes.
+enum FilterMode : int { kHash = 0, kBloom = 1 };
+
+// Counters in the per-launch device scratch block.
+struct DevCounters {
+    unsigned long long expansions;
+    unsigned long long distances;
+    unsigned long long estimates;
+    unsigned long long rerank;
+    unsigned int next_query;     // persistent-kernel work queue
+    unsigned int error_flags;    // ErrorFlag bits
+    unsigned int team_fallbacks; // queries that left the integer-exact path
+    unsigned int pad;
+};
+
+enum ErrorFlag : unsigned int {
+    kErrProbeBound = 1u,
+    kErrBadNode = 2u,
+};
+
+// Everything a search launch needs, passed by value.
+struct SearchParams {
+    // index (device pointers)
+    const float* vecs;          // [n][row_stride] f32, pad lanes zero
+    const uint32_t* adj;        // [n][degree] u32
+    uint64_t n;
+    uint32_t dim;
+    uint32_t row_stride;        // floats per stored row (dim rounded up to 4)
+    uint32_t degree;
+    // RaBitQ (device pointers, null unless mode rabitq)
+    const uint32_t* codes;      // [n][degree][wpp]
+    const float* factors;       // [n][3][degree]
+    const float* signs;         // [pdim]
+    uint32_t pdim;
+    uint32_t wpp;
+    // queries
+    const float* queries;       // [nq][dim] (stride dim)
+    uint32_t nq;
+    // search config
+    uint32_t topk;              // beam size T (topk_size)
+    uint32_t K;
+    uint32_t entry;
+    int32_t max_iterations;
+    // visited filter
+    uint32_t filter_slots;      // hash: table slots (pow2); bloom: bits (pow2)
+    uint32_t filter_limit;      // hash: reset when entries + degree would exceed
+    int32_t reset_interval;     // bloom reset period in expansions
+    // integer-exact distance path (kTeam): a query uses it only when all its
+    // values are integers with |q| <= team_qmax (negative: never)
+    float team_qmax;
+    // staging
+    uint32_t stage_rows;        // rows staged per round in kSeq mode
+    uint32_t stage_pitch;       // floats between staged rows (odd multiple of 4)
+    // per-warp shared-memory carve-up (bytes)
+    uint32_t smem_per_warp;
+    uint32_t off_filter;
+    uint32_t off_cids;
+    uint32_t off_cdist;
+    uint32_t off_stage;
+    uint32_t filter_words;      // u32 words of the filter table
+    // outputs
+    uint32_t* out_ids;          // [nq][K]
+    float* out_dists;           // [nq][K] or null
+    uint32_t* q_stats;          // [nq][2] (expansions, distances) or null
+    DevCounters* counters;
+};
+
+struct LaunchShape {
+    int regx;                   // beam registers per lane (beam capacity 32*regx)
+    int regy;                   // candidate registers per lane (degree <= 32*regy)
+    DistMode dmode;
+    FilterMode fmode;
+    int warps_per_block;
+    size_t smem_per_warp;
+};
+
+// Host launchers implemented in bs_search.cu.  Return cudaSuccess or the
+// launch error; shape.smem_per_warp is filled by plan_search.
+// Fills the regx/regy/smem fields of `shape` and the filter / staging /
+// shared-memory fields of `p` from the search configuration.  On an
+// unsupported configuration returns cudaErrorInvalidValue with a reason.
+cudaError_t plan_search(SearchParams& p, LaunchShape& shape, size_t max_smem_optin, char* why,
+                        size_t why_len);
+cudaError_t launch_search(const SearchParams& p, const LaunchShape& shape, int num_sms,
+                          cudaStream_t stream);
+cudaError_t launch_search_rabitq(const SearchParams& p, const LaunchShape& shape, int num_sms,
+                                 cudaStream_t stream);
+
+// Entry point (bs_entry.cu): centroid-nearest row, reference arithmetic.
+cudaError_t compute_entry_point(const float* vecs, uint64_t n, uint32_t dim, uint32_t row_stride,
+                                uint32_t* d_result, float* d_scratch, cudaStream_t stream);
+size_t entry_point_scratch_bytes(uint64_t n, uint32_t dim);
+
+}  // namespace bsb

@@ -1,0 +1,152 @@
+/*
+ * bsearch.h -- C ABI of the B200 graph beam-search library
+ * (libbsearch_b200.so).  Plain C types only: pointers, sizes, status codes.
+ *
+ * The reference (SophiaSun18/beam_search_collab) has no library boundary: its
+ * gpu_cli main() builds device copies of the graph and codebook and calls
+ * templated launchers directly.  Each entry point below names the reference
+ * piece it replaces (reference-relative file:line), so a host program written
+ * against the reference structure can bind this library one to one (see
+ * INTEGRATION.md for the binding a maintainer would add).
+ *
+ * Threading: an index is bound to one CUDA device.  bs_search may run
+ * concurrently on different streams; each call uses its own scratch.
+ * Errors: every call returns a bs_status; bs_last_error() gives the message
+ * of the calling thread's last failure.  The library never exits the process.
+ */
+#ifndef BSEARCH_H
+#define BSEARCH_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define BS_API __attribute__((visibility("default")))
+#else
+#define BS_API
+#endif
+
+#define BS_NO_NODE 0xFFFFFFFFu
+
+typedef enum bs_status {
+    BS_OK = 0,
+    BS_ERR_INVALID_ARGUMENT = 1, /* bad pointer, size, mode or config        */
+    BS_ERR_UNSUPPORTED = 2,      /* valid but outside this build's limits     */
+    BS_ERR_IO = 3,               /* file missing, short or malformed          */
+    BS_ERR_OUT_OF_MEMORY = 4,    /* host or device allocation failed          */
+    BS_ERR_CUDA = 5,             /* CUDA runtime error                        */
+    BS_ERR_KERNEL = 6            /* a kernel reported an internal error flag  */
+} bs_status;
+
+typedef struct bs_index bs_index;
+
+/* Host-resident graph: num_nodes rows of dim floats and of degree node ids
+ * (the CPUGraph fields of reference include/cpu_graph.hpp:24-28). */
+typedef struct bs_graph_desc {
+    uint64_t num_nodes;
+    int32_t dim;
+    int32_t degree;
+    const float* vectors;     /* [num_nodes][dim]    */
+    const uint32_t* edges;    /* [num_nodes][degree] */
+} bs_graph_desc;
+
+/* Host-resident RaBitQ data (CPURabitqData, reference include/rabitq.hpp:25-35).
+ * padded_dim = next power of two >= dim; words_per_plane = padded_dim/32. */
+typedef struct bs_rabitq_desc {
+    uint32_t entry_point;     /* BS_NO_NODE: none stored                      */
+    int32_t padded_dim;
+    const uint32_t* codes;    /* [num_nodes][degree][padded_dim/32]            */
+    const float* factors;     /* [num_nodes][3][degree] triple_x|factor_dq|factor_vq */
+    const float* signs;       /* [padded_dim]                                 */
+} bs_rabitq_desc;
+
+/* Search configuration: the "search" object of the reference JSON config
+ * (src/gpu_cli.cu:414-452).  mode is one of "base", "warp1", "warp2",
+ * "warp4", "warp8", "bwarp1", "bwarp2", "bwarp4", "bwarp8", "rabitq". */
+typedef struct bs_search_params {
+    const char* mode;
+    int32_t K;
+    uint32_t topk_size;
+    uint32_t filter_capacity;
+    int32_t max_iterations;
+    int32_t reset_interval;
+    uint32_t entry_point;     /* BS_NO_NODE: the index's default entry        */
+} bs_search_params;
+
+typedef struct bs_stats {
+    uint64_t expansions;      /* nodes expanded, all queries                  */
+    uint64_t distances;       /* exact L2 distances computed                  */
+    uint64_t estimates;       /* RaBitQ estimates computed                    */
+    uint64_t rerank;          /* exact distances in the RaBitQ final rerank   */
+    uint32_t error_flags;     /* kernel-side error bits (0 = none)            */
+    uint32_t entry_point;     /* entry node the search used                   */
+    uint32_t integer_exact;   /* 1: integer-exact distance path was used       */
+    uint32_t reserved;
+} bs_stats;
+
+/* Fills the reference defaults: mode "base", K 100, topk_size 256,
+ * filter_capacity 1024, max_iterations 1024, reset_interval 16
+ * (src/gpu_cli.cu:415-452). */
+BS_API void bs_search_params_default(bs_search_params* p);
+
+/* Replaces GPUGraph::GPUGraph(const CPUGraph&) (include/gpu_graph.cuh:126-141):
+ * copies vectors and edges to `device`.  The caller keeps its host arrays. */
+BS_API bs_status bs_index_create(const bs_graph_desc* desc, int device, bs_index** out);
+
+/* Replaces CPUGraph::load (include/cpu_graph.hpp:125-173) + GPUGraph: reads
+ * graph.bin (int32 n, int32 degree, uint32[n*degree]) and base .fvecs. */
+BS_API bs_status bs_index_load(const char* graph_bin, const char* base_fvecs, int device,
+                               bs_index** out);
+
+/* Replaces GPURabitq::GPURabitq(const CPURabitqData&) (include/rabitq.cuh:84-104). */
+BS_API bs_status bs_index_attach_rabitq(bs_index* index, const bs_rabitq_desc* desc);
+
+/* Replaces load_rabitq_codebook (include/rabitq.hpp:49-97) + GPURabitq. */
+BS_API bs_status bs_index_load_codebook(bs_index* index, const char* codebook_path);
+
+BS_API bs_status bs_index_info(const bs_index* index, uint64_t* num_nodes, int32_t* dim,
+                               int32_t* degree);
+
+/* Replaces compute_entry_point (src/gpu_cli.cu:55-83): row nearest to the
+ * float centroid, same arithmetic, computed on the GPU and cached. */
+BS_API bs_status bs_index_entry_point(bs_index* index, uint32_t* entry);
+
+/* The codebook's stored entry (medoid), BS_NO_NODE when absent or when no
+ * codebook is attached (reference src/gpu_cli.cu:436-437). */
+BS_API bs_status bs_index_rabitq_entry(const bs_index* index, uint32_t* entry);
+
+BS_API void bs_index_destroy(bs_index* index);
+
+/* Replaces run_base / run_warp / run_rabitq and their kernels
+ * (src/gpu_cli.cu:87-349): searches nq queries ([nq][dim] floats), writes
+ * ids [nq][K] (BS_NO_NODE past the end of the beam) and, when `dists` is not
+ * NULL, the matching squared L2 distances.  `queries`, `ids` and `dists` may
+ * each be host or device pointers; host buffers are copied inside the call,
+ * which then returns only when the results are in place.  With device
+ * buffers only and stats == NULL the call is asynchronous on `stream`
+ * (a cudaStream_t; NULL = legacy default stream). */
+BS_API bs_status bs_search(bs_index* index, const bs_search_params* params, const float* queries,
+                           uint32_t nq, uint32_t* ids, float* dists, bs_stats* stats,
+                           void* stream);
+
+/* Device buffers on the index's device (for callers that stage queries once
+ * and search many times, like the reference CLI's timed loop,
+ * src/gpu_cli.cu:400-421). */
+BS_API bs_status bs_device_alloc(const bs_index* index, size_t bytes, void** dptr);
+BS_API bs_status bs_device_free(const bs_index* index, void* dptr);
+BS_API bs_status bs_copy_to_device(const bs_index* index, void* dst, const void* src, size_t bytes);
+BS_API bs_status bs_copy_to_host(const bs_index* index, void* dst, const void* src, size_t bytes);
+BS_API bs_status bs_device_fill(const bs_index* index, void* dptr, int byte_value, size_t bytes);
+BS_API bs_status bs_synchronize(const bs_index* index, void* stream);
+
+BS_API const char* bs_last_error(void);
+BS_API const char* bs_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* BSEARCH_H */

@@ -1,0 +1,193 @@
+"""GPU parity: the CUDA search (through the C ABI) against the oracle and the
+reference's own golden results.  Integer ids must be identical row for row;
+distances are compared bit for bit (both distance paths reproduce the
+reference's fp32 sums exactly)."""
+import os
+
+import numpy as np
+import pytest
+
+import beam_search_collab_b200 as B
+import oracle as O
+import golden_sets as G
+
+pytestmark = pytest.mark.gpu
+
+EXACT_MODES = ("base", "warp1", "warp2", "warp4", "warp8")
+
+
+@pytest.fixture(scope="module")
+def indexes():
+    out = {}
+    for name in G.NAMES:
+        g = G.load(name)
+        ix = B.Index.from_arrays(g.base, g.edges)
+        if g.codebook_path:
+            ix.load_codebook(g.codebook_path)
+        out[name] = (g, ix)
+    yield out
+    for _, ix in out.values():
+        ix.close()
+
+
+@pytest.mark.parametrize("name", G.NAMES)
+def test_entry_point_matches_reference(indexes, name):
+    g, ix = indexes[name]
+    assert ix.entry_point() == g.entry
+
+
+@pytest.mark.parametrize("name", G.NAMES)
+@pytest.mark.parametrize("mode", EXACT_MODES)
+def test_exact_modes_match_reference_golden(indexes, name, mode):
+    g, ix = indexes[name]
+    for m, K, topk in g.runs("base"):
+        exp, run = g.expected(m, K, topk)
+        ids, dists, st = ix.search(g.queries, mode=mode, K=K, topk_size=topk)
+        same = (ids == exp).all(axis=1)
+        assert same.all(), f"{name} {mode} K={K} T={topk}: {np.count_nonzero(~same)}/{len(same)} rows differ"
+        ref = O.search(g.base, g.edges, g.queries, K=K, topk_size=topk, entry=g.entry)
+        assert np.array_equal(dists.view(np.uint32), ref.dists.view(np.uint32))
+        assert st.expansions == ref.stats.expansions
+        assert st.error_flags == 0
+
+
+@pytest.mark.parametrize("name", G.NAMES)
+def test_small_filter_forces_resets_and_stays_exact(indexes, name):
+    g, ix = indexes[name]
+    exp, _ = g.expected("base", 10, 64)
+    ids, _, st = ix.search(g.queries, mode="warp2", K=10, topk_size=64, filter_capacity=32)
+    assert (ids == exp).all()
+
+
+@pytest.mark.parametrize("name", G.NAMES)
+def test_distance_counter_matches_oracle_when_filter_never_resets(indexes, name):
+    g, ix = indexes[name]
+    ref = O.search(g.base, g.edges, g.queries, K=10, topk_size=64, entry=g.entry)
+    _, _, st = ix.search(g.queries, mode="warp4", K=10, topk_size=64, filter_capacity=1 << 14)
+    assert st.expansions == ref.stats.expansions
+    assert st.distances == ref.stats.distances
+
+
+@pytest.mark.parametrize("name", ["f48", "s96d64"])
+def test_rabitq_matches_reference_golden(indexes, name):
+    g, ix = indexes[name]
+    if not g.codebook_path:
+        pytest.skip("codebook not available")
+    cb = g.codebook()
+    for m, K, topk in g.runs("rabitq"):
+        exp, run = g.expected(m, K, topk)
+        ids, dists, st = ix.search(g.queries, mode="rabitq", K=K, topk_size=topk)
+        same = (ids == exp).all(axis=1)
+        assert same.all(), f"{name} rabitq K={K} T={topk}: {np.count_nonzero(~same)} rows differ"
+        ref = O.search(g.base, g.edges, g.queries, K=K, topk_size=topk, entry=run["search_entry"],
+                       mode="rabitq", codebook=cb)
+        assert np.array_equal(dists.view(np.uint32), ref.dists.view(np.uint32))
+        assert st.expansions == ref.stats.expansions
+        assert st.estimates == ref.stats.estimates
+
+
+@pytest.mark.parametrize("bits,reset", [(256, 16), (1024, 16), (4096, 32), (1 << 16, 0)])
+@pytest.mark.parametrize("mode", ["bwarp1", "bwarp4"])
+def test_bloom_modes_match_bloom_oracle(indexes, bits, reset, mode):
+    g, ix = indexes["f48"]
+    ids, dists, st = ix.search(g.queries, mode=mode, K=10, topk_size=64, filter_capacity=bits,
+                               reset_interval=reset)
+    ref = O.search(g.base, g.edges, g.queries, K=10, topk_size=64, entry=g.entry, mode="bloom",
+                   filter_bits=bits, reset_interval=reset)
+    assert np.array_equal(ids, ref.ids)
+    assert st.distances == ref.stats.distances
+
+
+def test_integer_path_and_sequential_path_agree(indexes, monkeypatch):
+    g, ix = indexes["i128"]
+    ids_t, d_t, st_t = ix.search(g.queries, mode="warp4", K=100, topk_size=256)
+    assert st_t.integer_exact == 1
+    monkeypatch.setenv("BSEARCH_FORCE_SEQ", "1")
+    ids_s, d_s, st_s = ix.search(g.queries, mode="warp4", K=100, topk_size=256)
+    assert st_s.integer_exact == 0
+    assert np.array_equal(ids_t, ids_s)
+    assert np.array_equal(d_t.view(np.uint32), d_s.view(np.uint32))
+
+
+def test_fractional_queries_leave_the_integer_path_and_stay_exact(indexes):
+    g, ix = indexes["i128"]
+    q = g.queries.copy()
+    q[::2] += np.float32(0.25)          # half of the queries are not integers
+    ids, dists, st = ix.search(q, mode="warp2", K=10, topk_size=64)
+    assert st.integer_exact == 0
+    ref = O.search(g.base, g.edges, q, K=10, topk_size=64, entry=g.entry)
+    assert np.array_equal(ids, ref.ids)
+    assert np.array_equal(dists.view(np.uint32), ref.dists.view(np.uint32))
+
+
+def test_device_and_host_buffers_agree(indexes):
+    torch = pytest.importorskip("torch")
+    g, ix = indexes["f48"]
+    ids_h, d_h, _ = ix.search(g.queries, mode="warp4", K=10, topk_size=64)
+    qd = torch.from_numpy(g.queries).cuda()
+    ids_d, d_d, _ = ix.search(qd, mode="warp4", K=10, topk_size=64)
+    torch.cuda.synchronize()
+    assert np.array_equal(ids_d.cpu().numpy().view(np.uint32), ids_h)
+    assert np.array_equal(d_d.cpu().numpy(), d_h)
+
+
+def test_k_larger_than_beam_pads_with_no_node(indexes):
+    g, ix = indexes["f48"]
+    ids, dists, _ = ix.search(g.queries[:8], mode="warp1", K=80, topk_size=32)
+    ref = O.search(g.base, g.edges, g.queries[:8], K=80, topk_size=32, entry=g.entry)
+    assert np.array_equal(ids, ref.ids)
+    assert (ids[:, 32:] == B.NO_NODE).all()
+    assert (dists[:, 32:] == np.finfo(np.float32).max).all()
+
+
+def test_max_iterations_zero_and_empty_batch(indexes):
+    g, ix = indexes["f48"]
+    ids, _, st = ix.search(g.queries[:4], mode="warp1", K=3, topk_size=64, max_iterations=0)
+    assert (ids[:, 0] == g.entry).all() and (ids[:, 1:] == B.NO_NODE).all()
+    assert st.expansions == 0
+    ids, _, st = ix.search(g.queries[:0], mode="warp1", K=3, topk_size=64)
+    assert ids.shape == (0, 3)
+
+
+def test_explicit_entry_point(indexes):
+    g, ix = indexes["f48"]
+    ids, _, st = ix.search(g.queries[:16], mode="warp4", K=10, topk_size=64, entry_point=5)
+    ref = O.search(g.base, g.edges, g.queries[:16], K=10, topk_size=64, entry=5)
+    assert st.entry_point == 5
+    assert np.array_equal(ids, ref.ids)
+
+
+def test_graph_with_padding_duplicates_and_missing_neighbours():
+    g = G.load("f48")
+    edges = g.edges.copy()
+    edges[:, 20:24] = 0                  # build_graph pads short lists with node 0
+    edges[::3, 30] = 0xFFFFFFFF          # empty slot
+    edges[::5, 31] = g.base.shape[0] + 7  # out-of-range id
+    ix = B.Index.from_arrays(g.base, edges)
+    try:
+        for mode in ("warp1", "bwarp2"):
+            ids, dists, _ = ix.search(g.queries, mode=mode, K=10, topk_size=64)
+            om = "base" if mode == "warp1" else "bloom"
+            ref = O.search(g.base, edges, g.queries, K=10, topk_size=64, entry=g.entry, mode=om)
+            assert np.array_equal(ids, ref.ids)
+            for row in ids:
+                v = row[row != B.NO_NODE]
+                assert len(set(v.tolist())) == len(v)
+    finally:
+        ix.close()
+
+
+def test_invalid_configurations_are_rejected(indexes):
+    g, ix = indexes["f48"]
+    with pytest.raises(B.BSearchError) as e:
+        ix.search(g.queries[:2], mode="warp3", K=10, topk_size=64)
+    assert "Unknown mode: warp3" in str(e.value)
+    with pytest.raises(B.BSearchError) as e:
+        ix.search(g.queries[:2], mode="warp1", K=10, topk_size=1024)
+    assert e.value.status == 2
+    with pytest.raises(B.BSearchError):
+        ix.search(g.queries[:2], mode="warp1", K=10, topk_size=64, entry_point=10 ** 6)
+    gi, ixi = indexes["i128"]
+    with pytest.raises(B.BSearchError) as e:
+        ixi.search(gi.queries[:2], mode="rabitq", K=10, topk_size=64)
+    assert "codebook" in str(e.value)
