@@ -40,8 +40,9 @@ struct bs_index {
     uint32_t row_stride = 0;
     float* d_vecs = nullptr;
     uint32_t* d_adj = nullptr;
-    bool int_exact = false;
-    float max_abs = 0.0f;
+    bool int_exact = false;      // every base value an integer
+    float min_val = 0.0f;        // range of the base values
+    float max_val = 0.0f;
     // RaBitQ
     bool has_rabitq = false;
     uint32_t rq_entry = BS_NO_NODE;
@@ -120,45 +121,55 @@ bool parse_mode(const char* m, ModeInfo& mi) {
     return false;
 }
 
-// Largest |value| and whether every value is an integer (multi-threaded scan
-// of the host array at index creation).
-void scan_values(const float* v, uint64_t count, bool& all_int, float& max_abs) {
+// Range of the values and whether every value is an integer (multi-threaded
+// scan of the host array at index creation).
+void scan_values(const float* v, uint64_t count, bool& all_int, float& min_val, float& max_val) {
     unsigned nt = std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
     if (count < (1u << 20)) nt = 1;
     std::vector<char> ints(nt, 1);
-    std::vector<float> maxes(nt, 0.0f);
+    std::vector<float> mins(nt, 0.0f), maxes(nt, 0.0f);
     std::vector<std::thread> th;
     const uint64_t per = (count + nt - 1) / nt;
     for (unsigned t = 0; t < nt; ++t) {
         th.emplace_back([&, t] {
             const uint64_t lo = per * t, hi = std::min(count, lo + per);
             bool ok = true;
-            float mx = 0.0f;
+            float mn = lo < hi ? v[lo] : 0.0f, mx = mn;
             for (uint64_t i = lo; i < hi; ++i) {
                 const float x = v[i];
-                ok = ok && (x == std::nearbyint(x));
-                const float a = std::fabs(x);
-                mx = a > mx ? a : mx;
-                if (!(a == a)) ok = false;
+                ok = ok && (x == std::nearbyint(x));   // false for NaN and inf
+                mn = x < mn ? x : mn;
+                mx = x > mx ? x : mx;
             }
             ints[t] = ok;
+            mins[t] = mn;
             maxes[t] = mx;
         });
     }
     for (auto& t : th) t.join();
     all_int = true;
-    max_abs = 0.0f;
+    min_val = mins[0];
+    max_val = maxes[0];
     for (unsigned t = 0; t < nt; ++t) {
+        if (per * t >= count) continue;
         all_int = all_int && ints[t];
-        max_abs = std::max(max_abs, maxes[t]);
+        min_val = std::min(min_val, mins[t]);
+        max_val = std::max(max_val, maxes[t]);
     }
 }
 
-// |q| bound that keeps dim * (|q| + |x|max)^2 <= 2^24 (all partial sums exact).
-float team_qmax_for(const bs_index* ix) {
-    if (!ix->int_exact) return -1.0f;
-    const double lim = std::floor(std::sqrt(16777216.0 / ix->dim) - ix->max_abs);
-    return lim >= 0.0 ? static_cast<float>(lim) : -1.0f;
+// Query value range for the integer-exact path: with B = floor(sqrt(2^24/dim))
+// every |q_d - x_d| <= B keeps dim * B^2 <= 2^24, so all partial sums of the
+// squared differences are exact integers.  Empty range (lo > hi) = never.
+void team_range_for(const bs_index* ix, float& lo, float& hi) {
+    lo = 1.0f;
+    hi = 0.0f;
+    if (!ix->int_exact) return;
+    const double B = std::floor(std::sqrt(16777216.0 / ix->dim));
+    const double l = static_cast<double>(ix->max_val) - B, h = static_cast<double>(ix->min_val) + B;
+    if (l > h) return;
+    lo = static_cast<float>(l);
+    hi = static_cast<float>(h);
 }
 
 bool force_seq() {
@@ -260,7 +271,15 @@ BS_API bs_status bs_index_create(const bs_graph_desc* desc, int device, bs_index
     }
     if (e == cudaSuccess) e = cudaMemcpy(ix->d_adj, desc->edges, ebytes, cudaMemcpyHostToDevice);
     if (e != cudaSuccess) { free_index(ix); return cuda_fail(e, "index upload"); }
-    scan_values(desc->vectors, static_cast<uint64_t>(ix->n) * ix->dim, ix->int_exact, ix->max_abs);
+    scan_values(desc->vectors, static_cast<uint64_t>(ix->n) * ix->dim, ix->int_exact, ix->min_val, ix->max_val);
+    // Per-call scratch comes from the device's stream-ordered pool: keep freed
+    // blocks cached instead of returning them at every synchronisation.
+    cudaMemPool_t pool;
+    if (cudaDeviceGetDefaultMemPool(&pool, device) == cudaSuccess) {
+        uint64_t keep = UINT64_MAX;
+        cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+    }
+    cudaGetLastError();
     *out = ix;
     return BS_OK;
 }
@@ -396,8 +415,9 @@ BS_API bs_status bs_search(bs_index* ix, const bs_search_params* prm, const floa
     p.max_iterations = prm->max_iterations;
     p.filter_slots = prm->filter_capacity;
     p.reset_interval = prm->reset_interval;
-    const bool use_team = !force_seq() && ix->int_exact && team_qmax_for(ix) >= 0.0f;
-    p.team_qmax = use_team ? team_qmax_for(ix) : -1.0f;
+    team_range_for(ix, p.team_qlo, p.team_qhi);
+    const bool use_team = !force_seq() && p.team_qlo <= p.team_qhi;
+    if (!use_team) { p.team_qlo = 1.0f; p.team_qhi = 0.0f; }
 
     LaunchShape shape{};
     shape.dmode = use_team ? bsb::kTeam : bsb::kSeq;
@@ -414,6 +434,7 @@ BS_API bs_status bs_search(bs_index* ix, const bs_search_params* prm, const floa
     }
     if (nq == 0) return BS_OK;
 
+    cudaError_t e0 = cudaSuccess;
     const bool q_dev = is_device_ptr(queries);
     const bool i_dev = is_device_ptr(ids);
     const bool d_dev = dists ? is_device_ptr(dists) : true;
@@ -426,6 +447,13 @@ BS_API bs_status bs_search(bs_index* ix, const bs_search_params* prm, const floa
     if (!i_dev) off += (obytes + 255) & ~static_cast<size_t>(255);
     const size_t d_off = off;
     if (dists && !d_dev) off += (obytes + 255) & ~static_cast<size_t>(255);
+    const size_t s_off = off;
+    if (mi.rabitq) {
+        uint64_t warps = 0;
+        e0 = bsb::rabitq_grid_warps(p, shape, ix->num_sms, warps);
+        if (e0 != cudaSuccess) return cuda_fail(e0, "rabitq launch shape");
+        off += static_cast<size_t>(warps) * p.spill_slots * sizeof(uint32_t);
+    }
 
     char* scratch = nullptr;
     cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&scratch), off, stream);
@@ -435,6 +463,7 @@ BS_API bs_status bs_search(bs_index* ix, const bs_search_params* prm, const floa
     p.queries = q_dev ? queries : reinterpret_cast<const float*>(scratch + q_off);
     p.out_ids = i_dev ? ids : reinterpret_cast<uint32_t*>(scratch + i_off);
     p.out_dists = dists ? (d_dev ? dists : reinterpret_cast<float*>(scratch + d_off)) : nullptr;
+    p.spill = mi.rabitq ? reinterpret_cast<uint32_t*>(scratch + s_off) : nullptr;
 
     e = cudaMemsetAsync(scratch, 0, sizeof(DevCounters), stream);
     if (e == cudaSuccess && !q_dev)

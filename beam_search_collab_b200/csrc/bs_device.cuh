@@ -178,6 +178,18 @@ __device__ __forceinline__ int hash_insert(uint32_t* tab, uint32_t mask, uint32_
     return 1;
 }
 
+__device__ __forceinline__ bool hash_contains(const uint32_t* tab, uint32_t mask, uint32_t shift,
+                                              uint32_t key) {
+    uint32_t h = hash_slot(key, shift);
+    for (uint32_t i = 0; i <= mask; ++i) {
+        const uint32_t v = tab[h];
+        if (v == key) return true;
+        if (v == kNoNode) return false;
+        h = (h + 1) & mask;
+    }
+    return false;
+}
+
 // Bloom filter with the three hashes of include/filter_bloom.cuh:25-38.
 __device__ __forceinline__ void bloom_hashes(uint32_t key, uint32_t mask, uint32_t (&h)[3]) {
     uint32_t a = key;

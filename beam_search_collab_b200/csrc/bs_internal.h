@@ -41,8 +41,8 @@ struct DevCounters {
 };
 
 enum ErrorFlag : unsigned int {
-    kErrProbeBound = 1u,
-    kErrBadNode = 2u,
+    kErrProbeBound = 1u,     // a visited-table probe ran the whole table
+    kErrSpillFull = 2u,      // a query overflowed its RaBitQ spill table
 };
 
 // Everything a search launch needs, passed by value.
@@ -72,9 +72,14 @@ struct SearchParams {
     uint32_t filter_slots;      // hash: table slots (pow2); bloom: bits (pow2)
     uint32_t filter_limit;      // hash: reset when entries + degree would exceed
     int32_t reset_interval;     // bloom reset period in expansions
+    // RaBitQ exact visited set, second level: one table of spill_slots u32 per
+    // resident warp in global memory, used once the shared table is full
+    uint32_t* spill;
+    uint32_t spill_slots;
     // integer-exact distance path (kTeam): a query uses it only when all its
-    // values are integers with |q| <= team_qmax (negative: never)
-    float team_qmax;
+    // values are integers in [team_qlo, team_qhi] (empty range: never)
+    float team_qlo;
+    float team_qhi;
     // staging
     uint32_t stage_rows;        // rows staged per round in kSeq mode
     uint32_t stage_pitch;       // floats between staged rows (odd multiple of 4)
@@ -112,6 +117,9 @@ cudaError_t launch_search(const SearchParams& p, const LaunchShape& shape, int n
                           cudaStream_t stream);
 cudaError_t launch_search_rabitq(const SearchParams& p, const LaunchShape& shape, int num_sms,
                                  cudaStream_t stream);
+// Resident warps of the RaBitQ launch for `shape` (sizes the spill tables).
+cudaError_t rabitq_grid_warps(const SearchParams& p, const LaunchShape& shape, int num_sms,
+                              uint64_t& warps);
 
 // Entry point (bs_entry.cu): centroid-nearest row, reference arithmetic.
 cudaError_t compute_entry_point(const float* vecs, uint64_t n, uint32_t dim, uint32_t row_stride,

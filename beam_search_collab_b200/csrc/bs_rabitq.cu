@@ -56,6 +56,10 @@ __global__ void __launch_bounds__(256) k_search_rabitq(const SearchParams p) {
     const uint32_t fshift = 32u - static_cast<uint32_t>(__popc(fmask));
     const unsigned lt_mask = (1u << lane) - 1u;
     unsigned err = 0;
+    const size_t gwarp = static_cast<size_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    uint32_t* gtab = p.spill + gwarp * p.spill_slots;
+    const uint32_t gmask = p.spill_slots - 1u;
+    const uint32_t gshift = 32u - static_cast<uint32_t>(__popc(gmask));
 
     for (;;) {
         unsigned qi = 0;
@@ -67,7 +71,7 @@ __global__ void __launch_bounds__(256) k_search_rabitq(const SearchParams p) {
         for (uint32_t d = lane; d < p.row_stride; d += 32) qsm[d] = d < p.dim ? __ldg(q + d) : 0.0f;
         for (uint32_t i = lane; i < p.filter_words; i += 32) filt[i] = kNoNode;
         __syncwarp();
-        const bool team_ok = DM == kTeam && query_integer_exact(qsm, p.dim, p.team_qmax);
+        const bool team_ok = DM == kTeam && query_integer_exact(qsm, p.dim, p.team_qlo, p.team_qhi);
         if (DM == kTeam && !team_ok && lane == 0) atomicAdd(&p.counters->team_fallbacks, 1u);
 
         // ---- rotate + quantise (include/cpu_search_rabitq.hpp:34-57)
@@ -121,7 +125,8 @@ __global__ void __launch_bounds__(256) k_search_rabitq(const SearchParams p) {
             beam[0] = make_key(cdist[0], p.entry);
             hash_insert(filt, fmask, fshift, p.entry, err);
         }
-        uint32_t filled = 1;
+        uint32_t filled = 1, gfilled = 0;
+        bool spilled = false;
         uint32_t E = 0, D = 1, EST = 0;
         __syncwarp();
 
@@ -181,25 +186,26 @@ __global__ void __launch_bounds__(256) k_search_rabitq(const SearchParams p) {
             }
             ++D;
 
-            // visited filter: marked when pushed (include/cpu_search_rabitq.hpp:131-135)
-            if (filled + deg > p.filter_limit) {
-                for (uint32_t i = lane; i < p.filter_words; i += 32) filt[i] = kNoNode;
-                __syncwarp();
-                uint32_t cnt = 0;
-#pragma unroll
-                for (int r = 0; r < RX; ++r) {
-                    const bool v = beam[r] != kEmptyKey;
-                    if (v) hash_insert(filt, fmask, fshift, key_id(beam[r]), err);
-                    cnt += __popc(__ballot_sync(kFull, v));
-                }
-                filled = cnt;
+            // visited set: marked when pushed and never forgotten
+            // (include/cpu_search_rabitq.hpp:131-135).  An estimate depends on
+            // the parent, so a forgotten node could come back with a smaller
+            // value; the set is therefore exact: the shared-memory table
+            // first, then this warp's table in global memory once it is full.
+            if (!spilled && filled + deg > p.filter_limit) {
+                spilled = true;
+                for (uint32_t i = lane; i < p.spill_slots; i += 32) gtab[i] = kNoNode;
                 __syncwarp();
             }
+            if (spilled && gfilled + deg > (p.spill_slots / 4u) * 3u) err |= kErrSpillFull;
             bool fresh[RY];
             float est[RY];
 #pragma unroll
             for (int r = 0; r < RY; ++r) {
-                fresh[r] = c[r] < p.n && hash_insert(filt, fmask, fshift, c[r], err) != 0;
+                if (!spilled)
+                    fresh[r] = c[r] < p.n && hash_insert(filt, fmask, fshift, c[r], err) != 0;
+                else
+                    fresh[r] = c[r] < p.n && !hash_contains(filt, fmask, fshift, c[r]) &&
+                               hash_insert(gtab, gmask, gshift, c[r], err) != 0;
                 est[r] = FLT_MAX;
                 if (fresh[r] && tx[r] != FLT_MAX) {
                     // include/cpu_search_rabitq.hpp:72-97
@@ -233,7 +239,7 @@ __global__ void __launch_bounds__(256) k_search_rabitq(const SearchParams p) {
             }
             __syncwarp();
             if (m) {
-                filled += m;
+                if (spilled) gfilled += m; else filled += m;
                 EST += m;
                 uint64_t cand[RY];
 #pragma unroll
@@ -319,11 +325,10 @@ KernelFn select_rq(int regx, int regy, int dm) {
     return nullptr;
 }
 
-}  // namespace
-
-cudaError_t launch_search_rabitq(const SearchParams& p, const LaunchShape& shape, int num_sms,
-                                 cudaStream_t stream) {
-    KernelFn fn = select_rq(shape.regx, shape.regy, shape.dmode);
+// Persistent grid: at most the resident capacity, at least one warp per query.
+cudaError_t rabitq_grid(const SearchParams& p, const LaunchShape& shape, int num_sms, KernelFn& fn,
+                        unsigned& grid) {
+    fn = select_rq(shape.regx, shape.regy, shape.dmode);
     if (!fn) return cudaErrorInvalidValue;
     const int threads = 32 * shape.warps_per_block;
     const size_t smem = static_cast<size_t>(shape.smem_per_warp) * shape.warps_per_block;
@@ -336,9 +341,30 @@ cudaError_t launch_search_rabitq(const SearchParams& p, const LaunchShape& shape
     if (per_sm < 1) return cudaErrorInvalidConfiguration;
     const uint64_t want = (static_cast<uint64_t>(p.nq) + shape.warps_per_block - 1) / shape.warps_per_block;
     const uint64_t cap = static_cast<uint64_t>(per_sm) * static_cast<uint64_t>(num_sms);
-    const unsigned grid = static_cast<unsigned>(want < cap ? want : cap);
+    grid = static_cast<unsigned>(want < cap ? want : cap);
+    return cudaSuccess;
+}
+
+}  // namespace
+
+cudaError_t rabitq_grid_warps(const SearchParams& p, const LaunchShape& shape, int num_sms,
+                              uint64_t& warps) {
+    KernelFn fn;
+    unsigned grid = 0;
+    const cudaError_t e = rabitq_grid(p, shape, num_sms, fn, grid);
+    warps = static_cast<uint64_t>(grid) * shape.warps_per_block;
+    return e;
+}
+
+cudaError_t launch_search_rabitq(const SearchParams& p, const LaunchShape& shape, int num_sms,
+                                 cudaStream_t stream) {
+    KernelFn fn;
+    unsigned grid = 0;
+    const cudaError_t e = rabitq_grid(p, shape, num_sms, fn, grid);
+    if (e != cudaSuccess) return e;
     if (grid == 0) return cudaSuccess;
-    fn<<<grid, threads, smem, stream>>>(p);
+    const size_t smem = static_cast<size_t>(shape.smem_per_warp) * shape.warps_per_block;
+    fn<<<grid, 32 * shape.warps_per_block, smem, stream>>>(p);
     return cudaGetLastError();
 }
 

@@ -9,14 +9,16 @@ namespace bsb {
 namespace dev {
 
 // Whole-warp test of the integer-exact condition for the query in smem:
-// every value an integer and |q| <= qmax, so that with the index's own bound
-// every partial sum of squared differences is an exactly representable
-// integer and the summation order cannot change a bit.
-__device__ __forceinline__ bool query_integer_exact(const float* qsm, uint32_t dim, float qmax) {
-    bool ok = qmax >= 0.0f;
+// every value an integer in [qlo, qhi].  The host derives that range from the
+// base vectors' own range so that every |q_d - x_d| <= B with
+// dim * B^2 <= 2^24: every product and partial sum is then an exactly
+// representable integer and the summation order cannot change a bit.
+__device__ __forceinline__ bool query_integer_exact(const float* qsm, uint32_t dim, float qlo,
+                                                    float qhi) {
+    bool ok = qlo <= qhi;
     for (uint32_t d = threadIdx.x & 31u; d < dim; d += 32) {
         const float v = qsm[d];
-        ok = ok && (v == rintf(v)) && (fabsf(v) <= qmax);
+        ok = ok && (v == rintf(v)) && (v >= qlo) && (v <= qhi);
     }
     return __all_sync(kFull, ok);
 }

@@ -60,7 +60,7 @@ __global__ void __launch_bounds__(256) k_search_l2(const SearchParams p) {
         for (uint32_t i = lane; i < p.filter_words; i += 32) filt[i] = (FM == kHash) ? kNoNode : 0u;
         if (lane == 0) cids[0] = p.entry;
         __syncwarp();
-        const bool team_ok = DM == kTeam && query_integer_exact(qsm, p.dim, p.team_qmax);
+        const bool team_ok = DM == kTeam && query_integer_exact(qsm, p.dim, p.team_qlo, p.team_qhi);
         if (DM == kTeam && !team_ok && lane == 0) atomicAdd(&p.counters->team_fallbacks, 1u);
 
         // seed: the entry point with its exact distance
@@ -254,7 +254,21 @@ cudaError_t plan_search(SearchParams& p, LaunchShape& shape, size_t max_smem_opt
     if (shape.regx < shape.regy) shape.regx = shape.regy;
 
     // visited filter
-    if (shape.fmode == kHash) {
+    if (p.codes != nullptr) {
+        // RaBitQ: exact, never-reset set -- a shared-memory table of
+        // filter_capacity slots (<= 3/4 load) that spills into a per-warp
+        // global table sized for every insert max_iterations expansions make.
+        const uint64_t need = (static_cast<uint64_t>(p.topk) + 2ull * p.degree) * 4ull / 3ull + 1;
+        const uint32_t slots = pow2_at_least(p.filter_slots > need ? p.filter_slots : need);
+        p.filter_slots = slots;
+        p.filter_limit = slots / 4u * 3u;
+        p.filter_words = slots;
+        const uint64_t inserts = 1ull + static_cast<uint64_t>(p.max_iterations > 0 ? p.max_iterations : 0) * p.degree;
+        uint64_t gs = pow2_at_least(inserts * 4ull / 3ull + 1ull);
+        if (gs < 1024u) gs = 1024u;
+        if (gs > 65536u) gs = 65536u;
+        p.spill_slots = static_cast<uint32_t>(gs);
+    } else if (shape.fmode == kHash) {
         // Room for the beam plus several rows between resets, at <= 3/4 load.
         const uint64_t need = (static_cast<uint64_t>(p.topk) + 4ull * p.degree) * 4ull / 3ull + 1;
         const uint32_t slots = pow2_at_least(p.filter_slots > need ? p.filter_slots : need);

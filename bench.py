@@ -1,0 +1,458 @@
+"""Benchmark: QPS at recall@10 >= 0.95 on the C2 workload.
+
+C2 = 1,000,000 x 128 integer-valued [0,255] base vectors (seeded mixture of
+1,024 Gaussians, ~30% zeros), 10,000 queries per GPU, degree-32 Vamana graph
+(beam 128, alpha 2.0, seed 1234 -- the reference build_graph settings),
+K = 10.  The operating point is the smallest beam (topk_size) whose
+recall@10 against the exact top-10 is >= 0.95; a "step" is one search of all
+of a GPU's queries at that point.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Arms
+  ours       : the CUDA search through the C ABI (lib/libbsearch_b200.so).
+               value = device-resident queries / results (kernel + counter
+               reset per step), L2 flushed by a 256 MiB write before every
+               timed step (outside the timed window).  e2e = the same search
+               through the same public call with pinned host buffers, H2D of
+               the queries and D2H of ids+dists inside the timed window.
+  reference  : the reference's own CPU search (CPUBaseSearch through
+               oracle/_ref/ref_search_omp, all host cores), same data, K and
+               topk; each step a bounded sample of the queries.
+
+Multi-GPU (torchrun, one rank per GPU): query sharding over a replicated
+index, no collective on the data path; every rank searches its own 10,000
+queries (weak scaling); value = all ranks' queries / max-over-ranks time.
+"""
+from __future__ import annotations
+
+import argparse
+import hashlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+DATA_DIR = os.path.join(ROOT, "bench_data")
+GRAPH_C2 = os.path.join(DATA_DIR, "c2", "graph.bin")
+TOPK_SWEEP = (16, 24, 32, 40, 48, 52, 56, 60, 64, 72, 80, 96, 128, 192, 256)
+TARGET_RECALL = 0.95
+K = 10
+NQ_PER_GPU = 10_000
+FLUSH_BYTES = 256 << 20
+
+
+# ------------------------------------------------------------------ helpers
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons during the timed region."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+        self.t = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "20"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+        if self.t:
+            self.t.join(timeout=2)
+
+    def summary(self):
+        sm, smax, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def c2_data(nq_total: int):
+    from beam_search_collab_b200 import datasets as ds
+    s = ds.gen_c2(n=1_000_000, nq=nq_total)
+    return s.base, s.queries
+
+
+def load_graph():
+    from beam_search_collab_b200 import datasets as ds
+    if not os.path.exists(GRAPH_C2):
+        raise SystemExit(f"missing {GRAPH_C2}: build it with the reference settings "
+                         "(degree 32, beam 128, alpha 2.0, seed 1234) over the C2 base vectors")
+    return ds.read_graph(GRAPH_C2)
+
+
+def gpu_ground_truth(base_t, q_t, k):
+    """Exact top-k ids by squared L2, ties by id (float64 on the GPU: exact for
+    these integer-valued vectors)."""
+    import torch
+    b64 = base_t.double()
+    bn = (b64 * b64).sum(1)
+    out = np.empty((q_t.shape[0], k), dtype=np.int64)
+    extra = 32
+    for s in range(0, q_t.shape[0], 512):
+        q = q_t[s:s + 512].double()
+        d = bn[None, :] - 2.0 * (q @ b64.T) + (q * q).sum(1, keepdim=True)
+        vals, idx = torch.topk(d, k + extra, dim=1, largest=False, sorted=True)
+        vals, idx = vals.cpu().numpy(), idx.cpu().numpy()
+        for r in range(idx.shape[0]):
+            o = np.lexsort((idx[r], vals[r]))
+            out[s + r] = idx[r][o][:k]
+    return out
+
+
+def recall_at_k(pred, gt, k=K):
+    hits = 0
+    for p, g in zip(pred[:, :k], gt[:, :k]):
+        hits += len(set(p.tolist()) & set(g.tolist()))
+    return hits / (gt.shape[0] * k)
+
+
+# --------------------------------------------------------------- our arm
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import beam_search_collab_b200 as B
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    t0 = time.time()
+    base, queries_all = c2_data(NQ_PER_GPU * world)
+    queries = queries_all[rank * NQ_PER_GPU:(rank + 1) * NQ_PER_GPU]
+    edges = load_graph()
+    log(f"[rank {rank}] data ready in {time.time() - t0:.1f}s: base {base.shape}, graph {edges.shape}")
+    ix = B.Index.from_arrays(base, edges, device=local_rank)
+    entry = ix.entry_point()
+
+    base_t = torch.from_numpy(base).to(dev)
+    q_std = torch.from_numpy(queries_all[:NQ_PER_GPU]).to(dev)
+    gt = gpu_ground_truth(base_t, q_std, K)
+    del base_t
+
+    # operating point: smallest beam reaching the recall target (same on every rank)
+    chosen, sweep = None, []
+    for T in ([args.topk] if args.topk else TOPK_SWEEP):
+        ids, _, st = ix.search(q_std, mode=args.mode, K=K, topk_size=T)
+        torch.cuda.synchronize()
+        r = recall_at_k(ids.cpu().numpy().astype(np.int64), gt)
+        sweep.append({"topk_size": T, "recall@10": round(r, 5)})
+        if r >= TARGET_RECALL:
+            chosen = T
+            break
+    if chosen is None:
+        chosen = sweep[-1]["topk_size"]
+    params = B.SearchParams(mode=args.mode, K=K, topk_size=chosen)
+
+    # per-query counters at the operating point (untimed) for the roofline
+    q_dev = torch.from_numpy(queries).to(dev)
+    ids_d = torch.empty((NQ_PER_GPU, K), dtype=torch.int32, device=dev)
+    dists_d = torch.empty((NQ_PER_GPU, K), dtype=torch.float32, device=dev)
+    _, _, st = ix.search(q_dev, params)
+    torch.cuda.synchronize()
+    dim, deg = base.shape[1], edges.shape[1]
+    alg_bytes = (NQ_PER_GPU * 4 * dim + st.expansions * 4 * deg + st.distances * 4 * dim
+                 + NQ_PER_GPU * 4 * K)
+
+    stream = torch.cuda.Stream(device=dev)
+    flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+
+    def step():
+        ix.search_raw(q_dev.data_ptr(), NQ_PER_GPU, ids_d.data_ptr(), dists_d.data_ptr(), params,
+                      stream=stream.cuda_stream)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            flush.zero_()
+            step()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    with ClockSampler(local_rank) as clk:
+        with torch.cuda.stream(stream):
+            for i in range(args.steps):
+                flush.zero_()                       # L2 flush, outside the timed window
+                ev[i][0].record(stream)
+                step()
+                ev[i][1].record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    step_ms = [a.elapsed_time(b) for a, b in ev]
+    t_ms = sum(step_ms)
+
+    # e2e through the same public call with pinned host buffers
+    hq = torch.from_numpy(queries).pin_memory()
+    hid = torch.empty((NQ_PER_GPU, K), dtype=torch.int32).pin_memory()
+    hdist = torch.empty((NQ_PER_GPU, K), dtype=torch.float32).pin_memory()
+    e2e_steps = max(3, min(args.steps, 10))
+    for _ in range(2):
+        ix.search_raw(hq.data_ptr(), NQ_PER_GPU, hid.data_ptr(), hdist.data_ptr(), params, stream=stream.cuda_stream)
+    ee = []
+    for _ in range(e2e_steps):
+        with torch.cuda.stream(stream):
+            flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        ix.search_raw(hq.data_ptr(), NQ_PER_GPU, hid.data_ptr(), hdist.data_ptr(), params, stream=stream.cuda_stream)
+        b.record(stream)
+        b.synchronize()
+        ee.append(a.elapsed_time(b))
+    e2e_ms = statistics.mean(ee)
+    assert np.array_equal(hid.numpy(), ids_d.cpu().numpy()), "e2e results differ from device-resident results"
+
+    # max over ranks
+    if world > 1:
+        t = torch.tensor([t_ms, e2e_ms], dtype=torch.float64, device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        t_ms, e2e_ms = float(t[0]), float(t[1])
+    ms_per_step = t_ms / args.steps
+    value = world * NQ_PER_GPU / (ms_per_step / 1e3)
+    e2e_value = world * NQ_PER_GPU / (e2e_ms / 1e3)
+
+    if rank != 0:
+        return None
+    peak, peak_kind = peaks()
+    achieved = alg_bytes / (statistics.mean(step_ms) / 1e3) / 1e9
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "traffic_k_search_l2_c2.json")
+    if os.path.exists(tp):
+        with open(tp) as f:
+            traffic = json.load(f).get("dram_bytes_per_launch")
+    line = {
+        "metric": "QPS at recall@10>=0.95",
+        "value": round(value, 1),
+        "unit": "queries/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_per_step, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic: seeded C2 mixture (1,024 Gaussians, ints 0..255), graph from the reference build_graph settings",
+        "config": {
+            "workload": "C2: 1M x 128 int-valued base, 10k queries per GPU, degree-32 Vamana, K=10",
+            "mode": args.mode, "K": K, "topk_size": chosen,
+            "recall@10": sweep[-1]["recall@10"] if chosen == sweep[-1]["topk_size"] else None,
+            "recall_sweep": sweep,
+            "entry_point": entry,
+            "distance_path": "integer-exact (8-lane teams)" if st.integer_exact else "sequential per lane",
+            "expansions_per_query": round(st.expansions / NQ_PER_GPU, 2),
+            "distances_per_query": round(st.distances / NQ_PER_GPU, 2),
+            "l2": "256 MiB write before every timed step (outside the timed window); index 640 MB > L2",
+            "parallelism": f"query-sharded dp{world}, replicated index",
+        },
+        "roofline": {
+            "bound": "hbm",
+            "achieved": round(achieved, 1),
+            "peak": peak,
+            "unit": "GB/s",
+            "frac": round(achieved / peak, 4),
+            "traffic": traffic,
+            "peak_kind": peak_kind,
+            "algorithmic_bytes_per_launch": int(alg_bytes),
+        },
+        "e2e": {"value": round(e2e_value, 1), "unit": "queries/s",
+                "h2d_bytes_per_step": int(NQ_PER_GPU * base.shape[1] * 4),
+                "d2h_bytes_per_step": int(NQ_PER_GPU * K * 8)},
+        "gpu_launches": args.steps,
+        "clocks": clk.summary(),
+    }
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(base, queries, edges, chosen, entry, sample=args.cpu_sample)
+    return line
+
+
+# ------------------------------------------------------ reference CPU arm
+
+def _write_inputs(tmp, base, queries, edges):
+    from beam_search_collab_b200 import datasets as ds
+    bp, qp = os.path.join(tmp, "base.fvecs"), os.path.join(tmp, "query.fvecs")
+    ds.write_fvecs(bp, base)
+    ds.write_fvecs(qp, queries)
+    return GRAPH_C2, bp, qp
+
+
+def _ref_search(paths, topk, entry, nq, threads=None):
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    g, b, q = paths
+    info, _ = O.run_ref_search(g, b, q, K=K, topk=topk, mode="base", threads=threads, nq=nq, entry=entry)
+    return info
+
+
+def cpu_baseline(base, queries, edges, topk, entry, sample=2000):
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    if O.ref_tool("ref_search_omp") is None:
+        return {"value": None, "unit": "queries/s", "cores": 0, "kind": "reference",
+                "sample": "unavailable: oracle/_ref/ref_search_omp not built"}
+    with tempfile.TemporaryDirectory() as tmp:
+        paths = _write_inputs(tmp, base, queries, edges)
+        info = _ref_search(paths, topk, entry, sample)
+    return {"value": round(info["qps"], 1), "unit": "queries/s", "cores": info["threads"], "kind": "reference",
+            "sample": f"first {info['nq']} of the 10k queries, CPUBaseSearch (reference include/cpu_search_base.hpp) "
+                      f"under OpenMP on all host threads, topk_size {topk}, K {K}"}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return None
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    if O.ref_tool("ref_search_omp") is None:
+        return {"impl": "reference", "unavailable": "oracle/_ref/ref_search_omp was not built from the reference tree"}
+    base, queries_all = c2_data(NQ_PER_GPU)
+    edges = load_graph()
+    topk = args.topk or 32
+    entry = O.entry_point(base)
+    with tempfile.TemporaryDirectory() as tmp:
+        paths = _write_inputs(tmp, base, queries_all, edges)
+        for _ in range(args.warmup):
+            _ref_search(paths, topk, entry, args.ref_sample)
+        infos = [_ref_search(paths, topk, entry, args.ref_sample) for _ in range(args.steps)]
+    secs = sum(i["seconds"] for i in infos)
+    nq = sum(i["nq"] for i in infos)
+    value = nq / secs
+    cores = infos[0]["threads"]
+    return {
+        "impl": "reference",
+        "metric": "QPS at recall@10>=0.95",
+        "value": round(value, 1),
+        "unit": "queries/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(1e3 * secs / args.steps, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic: seeded C2 mixture (1,024 Gaussians, ints 0..255), graph from the reference build_graph settings",
+        "config": {"workload": "C2: 1M x 128 int-valued base, 10k queries, degree-32 Vamana, K=10",
+                   "mode": "cpu base (CPUBaseSearch)", "K": K, "topk_size": topk,
+                   "sample_per_step": args.ref_sample},
+        "cpu_baseline": {"value": round(value, 1), "unit": "queries/s", "cores": cores, "kind": "reference",
+                         "sample": f"{args.ref_sample} queries per step"},
+        "e2e": {"value": round(value, 1), "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def profile_run(args):
+    """Minimal launch sequence for an ncu capture of the search kernel on the
+    full C2 workload: entry-point kernels, `warmup` searches, one search."""
+    import torch
+    import beam_search_collab_b200 as B
+    base, queries = c2_data(NQ_PER_GPU)
+    edges = load_graph()
+    ix = B.Index.from_arrays(base, edges)
+    ix.entry_point()
+    q = torch.from_numpy(queries).cuda()
+    params = B.SearchParams(mode=args.mode, K=K, topk_size=args.topk or 32)
+    for _ in range(args.warmup + 1):
+        ix.search(q, params)
+    torch.cuda.synchronize()
+    log("profile run done")
+
+
+# -------------------------------------------------------------------- main
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--mode", default="warp4")
+    ap.add_argument("--topk", type=int, default=0, help="fixed topk_size (0: sweep to the recall target)")
+    ap.add_argument("--cpu-sample", type=int, default=2000)
+    ap.add_argument("--ref-sample", type=int, default=1000)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-run", action="store_true",
+                    help="for ncu: build the index, run `--warmup` searches and one more, print nothing else")
+    args = ap.parse_args()
+    if args.profile_run:
+        profile_run(args)
+        return
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and args.impl == "ours":
+        import datetime
+        import torch
+        torch.cuda.set_device(local_rank)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                             device_id=torch.device("cuda", local_rank))
+    if args.impl == "reference":
+        line = run_reference(args, rank, world)
+    else:
+        line = run_ours(args, rank, world, local_rank)
+    if rank == 0 and line is not None:
+        print(json.dumps(line), flush=True)
+    if world > 1 and args.impl == "ours":
+        import torch
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

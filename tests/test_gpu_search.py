@@ -63,7 +63,7 @@ def test_small_filter_forces_resets_and_stays_exact(indexes, name):
 def test_distance_counter_matches_oracle_when_filter_never_resets(indexes, name):
     g, ix = indexes[name]
     ref = O.search(g.base, g.edges, g.queries, K=10, topk_size=64, entry=g.entry)
-    _, _, st = ix.search(g.queries, mode="warp4", K=10, topk_size=64, filter_capacity=1 << 14)
+    _, _, st = ix.search(g.queries, mode="warp1", K=10, topk_size=64, filter_capacity=1 << 14)
     assert st.expansions == ref.stats.expansions
     assert st.distances == ref.stats.distances
 
@@ -84,6 +84,17 @@ def test_rabitq_matches_reference_golden(indexes, name):
         assert np.array_equal(dists.view(np.uint32), ref.dists.view(np.uint32))
         assert st.expansions == ref.stats.expansions
         assert st.estimates == ref.stats.estimates
+
+
+@pytest.mark.parametrize("cap", [64, 1024, 1 << 13])
+def test_rabitq_visited_set_spill_stays_exact(indexes, cap):
+    g, ix = indexes["s96d64"]
+    if not g.codebook_path:
+        pytest.skip("codebook not available")
+    exp, _ = g.expected("rabitq", 10, 128)
+    ids, _, st = ix.search(g.queries, mode="rabitq", K=10, topk_size=128, filter_capacity=cap)
+    assert (ids == exp).all()
+    assert st.error_flags == 0
 
 
 @pytest.mark.parametrize("bits,reset", [(256, 16), (1024, 16), (4096, 32), (1 << 16, 0)])
