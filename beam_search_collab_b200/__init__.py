@@ -68,7 +68,8 @@ class Stats(ctypes.Structure):
 # Every symbol include/bsearch.h declares (checked by the CPU test suite).
 EXPORTS = ("bs_search_params_default", "bs_index_create", "bs_index_load", "bs_index_attach_rabitq",
            "bs_index_load_codebook", "bs_index_info", "bs_index_entry_point", "bs_index_rabitq_entry",
-           "bs_index_destroy", "bs_search", "bs_device_alloc", "bs_device_free", "bs_copy_to_device",
+           "bs_index_destroy", "bs_search", "bs_search_no_alloc", "bs_device_alloc", "bs_device_free",
+           "bs_copy_to_device",
            "bs_copy_to_host", "bs_device_fill", "bs_synchronize", "bs_last_error", "bs_version")
 
 _lib = None
@@ -97,6 +98,8 @@ def lib() -> ctypes.CDLL:
     L.bs_index_destroy.restype = None
     L.bs_search.argtypes = [vp, ctypes.POINTER(_Params), vp, ctypes.c_uint32, vp, vp,
                             ctypes.POINTER(Stats), vp]
+    L.bs_search_no_alloc.argtypes = [vp, ctypes.POINTER(_Params), vp, ctypes.c_uint32, vp, vp, vp]
+    L.bs_search_no_alloc.restype = st
     L.bs_device_alloc.argtypes = [vp, ctypes.c_size_t, ctypes.POINTER(vp)]
     L.bs_device_free.argtypes = [vp, vp]
     L.bs_copy_to_device.argtypes = [vp, vp, vp, ctypes.c_size_t]

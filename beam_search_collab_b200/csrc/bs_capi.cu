@@ -498,6 +498,152 @@ BS_API bs_status bs_search(bs_index* ix, const bs_search_params* prm, const floa
     return BS_OK;
 }
 
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free search (bs_search_no_alloc).
+//
+// Some callers cannot allocate device memory once they are running: a host
+// process that reserves the GPU's memory at start-up and forbids later
+// allocations (a serving process with a fixed memory budget, or a plugin that
+// lives inside a runtime owning all device memory through its own
+// allocator), or a latency-critical loop where cudaMalloc's possible
+// device-wide blocking, or its failure under memory pressure, is not
+// acceptable.  For them the search kernel's scratch -- its work-queue counter,
+// statistics and error flags, and on a device's first entry-point computation
+// the centroid -- lives in the fixed array below instead of in per-call
+// allocations.
+//
+// The array is a file-scope __device__ variable: every GPU that loads this
+// library holds one copy of kFixedScratchBytes until the process exits.  In
+// host code its name is only a host-side stand-in, never a device address, so
+// the device address is looked up once per device with cudaGetSymbolAddress
+// (with that device current) and passed to the kernels.
+static constexpr size_t kFixedScratchBytes = 16384;
+static constexpr size_t kFixedEntryOffset = 256;       // [0,256): search counters
+static constexpr uint32_t kFixedMaxQueries = 1u << 31;  // keeps the u32 work counter from wrapping
+static __device__ __align__(256) unsigned char g_fixed_scratch[kFixedScratchBytes];
+static_assert(sizeof(DevCounters) <= kFixedEntryOffset, "search counters must fit below the entry scratch");
+
+namespace {
+
+constexpr int kFixedMaxDevices = 64;
+std::mutex g_fixed_mu;
+unsigned char* g_fixed_addr[kFixedMaxDevices] = {};
+
+// Device address of g_fixed_scratch on `device`, which must be current.
+bs_status fixed_scratch(int device, unsigned char** out) {
+    if (device < 0 || device >= kFixedMaxDevices)
+        return fail(BS_ERR_UNSUPPORTED, "device %d is beyond the %d devices the fixed scratch tracks", device,
+                    kFixedMaxDevices);
+    std::lock_guard<std::mutex> lk(g_fixed_mu);
+    if (!g_fixed_addr[device]) {
+        void* addr = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&addr, g_fixed_scratch);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_fixed_scratch)");
+        g_fixed_addr[device] = static_cast<unsigned char*>(addr);
+    }
+    *out = g_fixed_addr[device];
+    return BS_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+BS_API bs_status bs_search_no_alloc(bs_index* ix, const bs_search_params* prm, const float* queries, uint32_t nq,
+                                    uint32_t* ids, float* dists, void* stream_) {
+    if (!ix || !prm) return fail(BS_ERR_INVALID_ARGUMENT, "index or params is NULL");
+    ModeInfo mi;
+    if (!parse_mode(prm->mode, mi)) return fail(BS_ERR_INVALID_ARGUMENT, "Unknown mode: %s", prm->mode ? prm->mode : "(null)");
+    if (mi.rabitq)
+        return fail(BS_ERR_UNSUPPORTED,
+                    "rabitq needs per-warp visited-set spill tables larger than the %zu-byte fixed scratch; use bs_search",
+                    kFixedScratchBytes);
+    if (prm->K <= 0) return fail(BS_ERR_INVALID_ARGUMENT, "K must be positive");
+    if (prm->topk_size == 0) return fail(BS_ERR_INVALID_ARGUMENT, "topk_size must be positive");
+    if (prm->max_iterations < 0) return fail(BS_ERR_INVALID_ARGUMENT, "max_iterations must be >= 0");
+    if (nq > kFixedMaxQueries)
+        return fail(BS_ERR_UNSUPPORTED, "nq %u exceeds the fixed-scratch limit of %u queries per call", nq,
+                    kFixedMaxQueries);
+    if (nq > 0 && (!queries || !ids)) return fail(BS_ERR_INVALID_ARGUMENT, "queries or ids is NULL");
+
+    DeviceGuard g(ix->device);
+    if (!g.ok) return fail(BS_ERR_CUDA, "cannot select device %d", ix->device);
+    if (nq > 0 && (!is_device_ptr(queries) || !is_device_ptr(ids) || (dists && !is_device_ptr(dists))))
+        return fail(BS_ERR_INVALID_ARGUMENT,
+                    "bs_search_no_alloc takes device pointers only (host buffers would need staging memory)");
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+    unsigned char* scratch = nullptr;
+    bs_status s = fixed_scratch(ix->device, &scratch);
+    if (s != BS_OK) return s;
+
+    uint32_t entry = prm->entry_point;
+    if (entry == BS_NO_NODE) {
+        std::lock_guard<std::mutex> lk(ix->mu);
+        if (!ix->entry_valid) {
+            // centroid (dim floats) + packed argmin key, then the u32 result
+            const size_t need = bsb::entry_point_scratch_bytes(ix->n, ix->dim) + 8;
+            if (kFixedEntryOffset + need > kFixedScratchBytes)
+                return fail(BS_ERR_UNSUPPORTED,
+                            "dim %d is too large to compute the entry point in the %zu-byte fixed scratch; "
+                            "pass entry_point or call bs_index_entry_point first",
+                            ix->dim, kFixedScratchBytes);
+            unsigned char* es = scratch + kFixedEntryOffset;
+            uint32_t* d_out = reinterpret_cast<uint32_t*>(es + need - 8);
+            cudaError_t e = bsb::compute_entry_point(ix->d_vecs, ix->n, ix->dim, ix->row_stride, d_out,
+                                                     reinterpret_cast<float*>(es), stream);
+            uint32_t h = 0;
+            if (e == cudaSuccess) e = cudaMemcpyAsync(&h, d_out, 4, cudaMemcpyDeviceToHost, stream);
+            if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+            if (e != cudaSuccess) return cuda_fail(e, "entry point kernel");
+            ix->entry = h;
+            ix->entry_valid = true;
+        }
+        entry = ix->entry;
+    }
+    if (entry >= ix->n) return fail(BS_ERR_INVALID_ARGUMENT, "entry point %u out of range", entry);
+    if (nq == 0) return BS_OK;
+
+    SearchParams p{};
+    p.vecs = ix->d_vecs;
+    p.adj = ix->d_adj;
+    p.n = ix->n;
+    p.dim = static_cast<uint32_t>(ix->dim);
+    p.row_stride = ix->row_stride;
+    p.degree = static_cast<uint32_t>(ix->degree);
+    p.queries = queries;
+    p.nq = nq;
+    p.topk = prm->topk_size;
+    p.K = static_cast<uint32_t>(prm->K);
+    p.entry = entry;
+    p.max_iterations = prm->max_iterations;
+    p.filter_slots = prm->filter_capacity;
+    p.reset_interval = prm->reset_interval;
+    team_range_for(ix, p.team_qlo, p.team_qhi);
+    const bool use_team = !force_seq() && p.team_qlo <= p.team_qhi;
+    if (!use_team) { p.team_qlo = 1.0f; p.team_qhi = 0.0f; }
+    p.out_ids = ids;
+    p.out_dists = dists;
+    p.counters = reinterpret_cast<DevCounters*>(scratch);
+
+    LaunchShape shape{};
+    shape.dmode = use_team ? bsb::kTeam : bsb::kSeq;
+    shape.fmode = mi.fmode;
+    shape.warps_per_block = mi.warps;
+    char why[256] = {0};
+    if (bsb::plan_search(p, shape, ix->smem_optin, why, sizeof(why)) != cudaSuccess)
+        return fail(BS_ERR_UNSUPPORTED, "%s", why);
+
+    // the array keeps the previous call's contents: the work queue and the
+    // counters must start from zero
+    cudaError_t e = cudaMemsetAsync(scratch, 0, sizeof(DevCounters), stream);
+    if (e != cudaSuccess) return cuda_fail(e, "fixed scratch reset");
+    e = bsb::launch_search(p, shape, ix->num_sms, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "search launch");
+    return BS_OK;
+}
+
 BS_API bs_status bs_device_alloc(const bs_index* ix, size_t bytes, void** dptr) {
     if (!ix || !dptr) return fail(BS_ERR_INVALID_ARGUMENT, "index or dptr is NULL");
     DeviceGuard g(ix->device);

@@ -133,6 +133,31 @@ BS_API bs_status bs_search(bs_index* index, const bs_search_params* params, cons
                            uint32_t nq, uint32_t* ids, float* dists, bs_stats* stats,
                            void* stream);
 
+/* No counterpart in the reference.  The same search as bs_search for the
+ * exact and Bloom modes (every mode but "rabitq"), for callers that cannot
+ * allocate device memory while they run -- a process that reserves the GPU's
+ * memory at start-up and forbids later allocations (fixed-budget serving, a
+ * plugin inside a runtime that owns all device memory), or a loop where an
+ * allocation's possible blocking or failure is not acceptable.  It calls no
+ * cudaMalloc/cudaFree or allocating routine: the kernel's scratch (work
+ * counter, statistics, error flags; the centroid when the entry point is
+ * first computed) lives in one 16 KiB file-scope device array that every GPU
+ * loading the library holds until the process exits.
+ *   - queries, ids and dists (NULL allowed) must be device pointers;
+ *   - nq <= 2^31; "rabitq" is rejected (its visited-set spill tables need more
+ *     than the fixed scratch), as is computing the entry point for
+ *     dim > 4028 (pass entry_point or call bs_index_entry_point first);
+ *   - the first call on a device looks up the array's device address, and if
+ *     neither entry_point nor a cached entry is available it computes the
+ *     entry point and synchronises `stream`; make that first call before any
+ *     stream capture;
+ *   - all calls share the one array, which keeps the last call's contents
+ *     (the counters are cleared at the start of every call): calls that
+ *     overlap on the GPU race, so serialise them (one stream, or events);
+ *   - asynchronous on `stream`; no statistics are returned. */
+BS_API bs_status bs_search_no_alloc(bs_index* index, const bs_search_params* params, const float* queries,
+                                    uint32_t nq, uint32_t* ids, float* dists, void* stream);
+
 /* Device buffers on the index's device (for callers that stage queries once
  * and search many times, like the reference CLI's timed loop,
  * src/gpu_cli.cu:400-421). */
