@@ -59,10 +59,10 @@ class Stats(ctypes.Structure):
     _fields_ = [("expansions", ctypes.c_uint64), ("distances", ctypes.c_uint64),
                 ("estimates", ctypes.c_uint64), ("rerank", ctypes.c_uint64),
                 ("error_flags", ctypes.c_uint32), ("entry_point", ctypes.c_uint32),
-                ("integer_exact", ctypes.c_uint32), ("reserved", ctypes.c_uint32)]
+                ("integer_exact", ctypes.c_uint32), ("row_bytes", ctypes.c_uint32)]
 
     def as_dict(self):
-        return {k: getattr(self, k) for k, _ in self._fields_ if k != "reserved"}
+        return {k: getattr(self, k) for k, _ in self._fields_}
 
 
 # Every symbol include/bsearch.h declares (checked by the CPU test suite).

@@ -38,7 +38,10 @@ struct bs_index {
     int32_t dim = 0;
     int32_t degree = 0;
     uint32_t row_stride = 0;
-    float* d_vecs = nullptr;
+    float* d_vecs = nullptr;     // f32 rows, or null when stored as bytes
+    bool u8 = false;             // rows stored as an exact u8 copy
+    uint32_t row_bytes = 0;
+    uint8_t* d_vecs8 = nullptr;
     uint32_t* d_adj = nullptr;
     bool int_exact = false;      // every base value an integer
     float min_val = 0.0f;        // range of the base values
@@ -177,10 +180,79 @@ bool force_seq() {
     return e && e[0] && e[0] != '0';
 }
 
+// BSEARCH_STORAGE=f32 keeps f32 rows even for byte-valued data (lets the
+// tests compare both storages).
+bool storage_f32_forced() {
+    const char* e = std::getenv("BSEARCH_STORAGE");
+    return e && std::strcmp(e, "f32") == 0;
+}
+
+// rows of dim floats (integers in [0,255]) -> rows of row_bytes bytes, zero pad
+void pack_u8_rows(const float* v, uint64_t n, int32_t dim, uint32_t row_bytes, uint8_t* out) {
+    unsigned nt = std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
+    if (n < (1u << 16)) nt = 1;
+    std::vector<std::thread> th;
+    const uint64_t per = (n + nt - 1) / nt;
+    for (unsigned t = 0; t < nt; ++t) {
+        th.emplace_back([=] {
+            const uint64_t lo = per * t, hi = std::min(n, lo + per);
+            for (uint64_t i = lo; i < hi; ++i)
+                for (int32_t d = 0; d < dim; ++d)
+                    out[i * row_bytes + d] = static_cast<uint8_t>(v[i * dim + d]);
+        });
+    }
+    for (auto& t : th) t.join();
+}
+
+cudaError_t entry_kernels(const bs_index* ix, uint32_t* d_out, float* scratch, cudaStream_t stream) {
+    return ix->u8 ? bsb::compute_entry_point_u8(ix->d_vecs8, ix->n, ix->dim, ix->row_bytes, d_out, scratch, stream)
+                  : bsb::compute_entry_point(ix->d_vecs, ix->n, ix->dim, ix->row_stride, d_out, scratch, stream);
+}
+
+// Search parameters shared by bs_search and bs_search_no_alloc (everything
+// but the output, query and scratch pointers).
+void fill_params(const bs_index* ix, const ModeInfo& mi, const bs_search_params* prm, uint32_t entry,
+                 SearchParams& p, LaunchShape& shape) {
+    p = SearchParams{};
+    p.vecs = ix->d_vecs;
+    p.vecs8 = ix->d_vecs8;
+    p.row_bytes = ix->row_bytes;
+    p.adj = ix->d_adj;
+    p.n = ix->n;
+    p.dim = static_cast<uint32_t>(ix->dim);
+    p.row_stride = ix->row_stride;
+    p.degree = static_cast<uint32_t>(ix->degree);
+    if (mi.rabitq) {
+        p.codes = ix->d_codes;
+        p.factors = ix->d_factors;
+        p.signs = ix->d_signs;
+        p.pdim = static_cast<uint32_t>(ix->pdim);
+        p.wpp = static_cast<uint32_t>(ix->pdim) / 32u;
+    }
+    p.topk = prm->topk_size;
+    p.K = static_cast<uint32_t>(prm->K);
+    p.entry = entry;
+    p.max_iterations = prm->max_iterations;
+    p.filter_slots = prm->filter_capacity;
+    p.reset_interval = prm->reset_interval;
+    team_range_for(ix, p.team_qlo, p.team_qhi);
+    if (ix->u8) {   // byte kernels need query bytes too
+        p.team_qlo = std::max(p.team_qlo, 0.0f);
+        p.team_qhi = std::min(p.team_qhi, 255.0f);
+    }
+    if (force_seq()) { p.team_qlo = 1.0f; p.team_qhi = 0.0f; }
+    shape = LaunchShape{};
+    if (ix->u8) shape.dmode = bsb::kU8;
+    else shape.dmode = p.team_qlo <= p.team_qhi ? bsb::kTeam : bsb::kSeq;
+    shape.fmode = mi.fmode;
+    shape.warps_per_block = mi.warps;
+}
+
 void free_index(bs_index* ix) {
     if (!ix) return;
     DeviceGuard g(ix->device);
     cudaFree(ix->d_vecs);
+    cudaFree(ix->d_vecs8);
     cudaFree(ix->d_adj);
     cudaFree(ix->d_codes);
     cudaFree(ix->d_factors);
@@ -196,8 +268,7 @@ bs_status ensure_entry(bs_index* ix) {
     cudaError_t e = cudaMalloc(&scratch, bytes);
     if (e != cudaSuccess) return cuda_fail(e, "entry point scratch");
     uint32_t* d_out = reinterpret_cast<uint32_t*>(static_cast<char*>(scratch) + bytes - 8);
-    e = bsb::compute_entry_point(ix->d_vecs, ix->n, ix->dim, ix->row_stride, d_out,
-                                 static_cast<float*>(scratch), nullptr);
+    e = entry_kernels(ix, d_out, static_cast<float*>(scratch), nullptr);
     uint32_t h = 0;
     if (e == cudaSuccess) e = cudaMemcpy(&h, d_out, 4, cudaMemcpyDeviceToHost);
     cudaFree(scratch);
@@ -256,22 +327,41 @@ BS_API bs_status bs_index_create(const bs_graph_desc* desc, int device, bs_index
     ix->num_sms = prop.multiProcessorCount;
     ix->smem_optin = prop.sharedMemPerBlockOptin;
 
-    const size_t vbytes = static_cast<size_t>(ix->n) * ix->row_stride * sizeof(float);
+    scan_values(desc->vectors, static_cast<uint64_t>(ix->n) * ix->dim, ix->int_exact, ix->min_val, ix->max_val);
+    // Exact byte copy when every value is an integer in [0,255] (SIFT-like
+    // data): a quarter of the HBM bytes per gathered row, integer distances.
+    ix->u8 = ix->int_exact && ix->min_val >= 0.0f && ix->max_val <= 255.0f && !storage_f32_forced();
+    ix->row_bytes = (static_cast<uint32_t>(desc->dim) + 15u) & ~15u;
+
     const size_t ebytes = static_cast<size_t>(ix->n) * ix->degree * sizeof(uint32_t);
-    if ((e = cudaMalloc(&ix->d_vecs, vbytes)) != cudaSuccess) { free_index(ix); return cuda_fail(e, "vectors"); }
     if ((e = cudaMalloc(&ix->d_adj, ebytes)) != cudaSuccess) { free_index(ix); return cuda_fail(e, "adjacency"); }
-    if (ix->row_stride == static_cast<uint32_t>(ix->dim)) {
-        e = cudaMemcpy(ix->d_vecs, desc->vectors, vbytes, cudaMemcpyHostToDevice);
+    if (ix->u8) {
+        const size_t vbytes = static_cast<size_t>(ix->n) * ix->row_bytes;
+        std::vector<uint8_t> packed;
+        try {
+            packed.assign(vbytes, 0);
+        } catch (...) {
+            free_index(ix);
+            return fail(BS_ERR_OUT_OF_MEMORY, "host staging for the byte copy");
+        }
+        pack_u8_rows(desc->vectors, ix->n, ix->dim, ix->row_bytes, packed.data());
+        if ((e = cudaMalloc(&ix->d_vecs8, vbytes)) != cudaSuccess) { free_index(ix); return cuda_fail(e, "vectors"); }
+        e = cudaMemcpy(ix->d_vecs8, packed.data(), vbytes, cudaMemcpyHostToDevice);
     } else {
-        e = cudaMemset(ix->d_vecs, 0, vbytes);
-        if (e == cudaSuccess)
-            e = cudaMemcpy2D(ix->d_vecs, ix->row_stride * sizeof(float), desc->vectors,
-                             ix->dim * sizeof(float), ix->dim * sizeof(float), ix->n,
-                             cudaMemcpyHostToDevice);
+        const size_t vbytes = static_cast<size_t>(ix->n) * ix->row_stride * sizeof(float);
+        if ((e = cudaMalloc(&ix->d_vecs, vbytes)) != cudaSuccess) { free_index(ix); return cuda_fail(e, "vectors"); }
+        if (ix->row_stride == static_cast<uint32_t>(ix->dim)) {
+            e = cudaMemcpy(ix->d_vecs, desc->vectors, vbytes, cudaMemcpyHostToDevice);
+        } else {
+            e = cudaMemset(ix->d_vecs, 0, vbytes);
+            if (e == cudaSuccess)
+                e = cudaMemcpy2D(ix->d_vecs, ix->row_stride * sizeof(float), desc->vectors,
+                                 ix->dim * sizeof(float), ix->dim * sizeof(float), ix->n,
+                                 cudaMemcpyHostToDevice);
+        }
     }
     if (e == cudaSuccess) e = cudaMemcpy(ix->d_adj, desc->edges, ebytes, cudaMemcpyHostToDevice);
     if (e != cudaSuccess) { free_index(ix); return cuda_fail(e, "index upload"); }
-    scan_values(desc->vectors, static_cast<uint64_t>(ix->n) * ix->dim, ix->int_exact, ix->min_val, ix->max_val);
     // Per-call scratch comes from the device's stream-ordered pool: keep freed
     // blocks cached instead of returning them at every synchronisation.
     cudaMemPool_t pool;
@@ -394,35 +484,11 @@ BS_API bs_status bs_search(bs_index* ix, const bs_search_params* prm, const floa
     }
     if (entry >= ix->n) return fail(BS_ERR_INVALID_ARGUMENT, "entry point %u out of range", entry);
 
-    SearchParams p{};
-    p.vecs = ix->d_vecs;
-    p.adj = ix->d_adj;
-    p.n = ix->n;
-    p.dim = static_cast<uint32_t>(ix->dim);
-    p.row_stride = ix->row_stride;
-    p.degree = static_cast<uint32_t>(ix->degree);
-    if (mi.rabitq) {
-        p.codes = ix->d_codes;
-        p.factors = ix->d_factors;
-        p.signs = ix->d_signs;
-        p.pdim = static_cast<uint32_t>(ix->pdim);
-        p.wpp = static_cast<uint32_t>(ix->pdim) / 32u;
-    }
+    SearchParams p;
+    LaunchShape shape;
+    fill_params(ix, mi, prm, entry, p, shape);
     p.nq = nq;
-    p.topk = prm->topk_size;
-    p.K = static_cast<uint32_t>(prm->K);
-    p.entry = entry;
-    p.max_iterations = prm->max_iterations;
-    p.filter_slots = prm->filter_capacity;
-    p.reset_interval = prm->reset_interval;
-    team_range_for(ix, p.team_qlo, p.team_qhi);
-    const bool use_team = !force_seq() && p.team_qlo <= p.team_qhi;
-    if (!use_team) { p.team_qlo = 1.0f; p.team_qhi = 0.0f; }
-
-    LaunchShape shape{};
-    shape.dmode = use_team ? bsb::kTeam : bsb::kSeq;
-    shape.fmode = mi.fmode;
-    shape.warps_per_block = mi.warps;
+    const bool use_team = p.team_qlo <= p.team_qhi;
     char why[256] = {0};
     if (bsb::plan_search(p, shape, ix->smem_optin, why, sizeof(why)) != cudaSuccess)
         return fail(BS_ERR_UNSUPPORTED, "%s", why);
@@ -431,6 +497,7 @@ BS_API bs_status bs_search(bs_index* ix, const bs_search_params* prm, const floa
         std::memset(stats, 0, sizeof(*stats));
         stats->entry_point = entry;
         stats->integer_exact = use_team ? 1u : 0u;
+        stats->row_bytes = ix->u8 ? ix->row_bytes : ix->row_stride * 4u;
     }
     if (nq == 0) return BS_OK;
 
@@ -591,8 +658,7 @@ BS_API bs_status bs_search_no_alloc(bs_index* ix, const bs_search_params* prm, c
                             ix->dim, kFixedScratchBytes);
             unsigned char* es = scratch + kFixedEntryOffset;
             uint32_t* d_out = reinterpret_cast<uint32_t*>(es + need - 8);
-            cudaError_t e = bsb::compute_entry_point(ix->d_vecs, ix->n, ix->dim, ix->row_stride, d_out,
-                                                     reinterpret_cast<float*>(es), stream);
+            cudaError_t e = entry_kernels(ix, d_out, reinterpret_cast<float*>(es), stream);
             uint32_t h = 0;
             if (e == cudaSuccess) e = cudaMemcpyAsync(&h, d_out, 4, cudaMemcpyDeviceToHost, stream);
             if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
@@ -605,32 +671,14 @@ BS_API bs_status bs_search_no_alloc(bs_index* ix, const bs_search_params* prm, c
     if (entry >= ix->n) return fail(BS_ERR_INVALID_ARGUMENT, "entry point %u out of range", entry);
     if (nq == 0) return BS_OK;
 
-    SearchParams p{};
-    p.vecs = ix->d_vecs;
-    p.adj = ix->d_adj;
-    p.n = ix->n;
-    p.dim = static_cast<uint32_t>(ix->dim);
-    p.row_stride = ix->row_stride;
-    p.degree = static_cast<uint32_t>(ix->degree);
+    SearchParams p;
+    LaunchShape shape;
+    fill_params(ix, mi, prm, entry, p, shape);
     p.queries = queries;
     p.nq = nq;
-    p.topk = prm->topk_size;
-    p.K = static_cast<uint32_t>(prm->K);
-    p.entry = entry;
-    p.max_iterations = prm->max_iterations;
-    p.filter_slots = prm->filter_capacity;
-    p.reset_interval = prm->reset_interval;
-    team_range_for(ix, p.team_qlo, p.team_qhi);
-    const bool use_team = !force_seq() && p.team_qlo <= p.team_qhi;
-    if (!use_team) { p.team_qlo = 1.0f; p.team_qhi = 0.0f; }
     p.out_ids = ids;
     p.out_dists = dists;
     p.counters = reinterpret_cast<DevCounters*>(scratch);
-
-    LaunchShape shape{};
-    shape.dmode = use_team ? bsb::kTeam : bsb::kSeq;
-    shape.fmode = mi.fmode;
-    shape.warps_per_block = mi.warps;
     char why[256] = {0};
     if (bsb::plan_search(p, shape, ix->smem_optin, why, sizeof(why)) != cudaSuccess)
         return fail(BS_ERR_UNSUPPORTED, "%s", why);

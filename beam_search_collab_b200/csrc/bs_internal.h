@@ -17,7 +17,13 @@ namespace bsb {
 //          Chosen only when every base and query value is an integer small
 //          enough that all partial sums are exact in fp32, in which case any
 //          order gives the same bits.
-enum DistMode : int { kSeq = 0, kTeam = 1 };
+//   kU8  : rows stored as u8 (every base value an integer in [0,255]; the
+//          copy is exact).  Integer queries in range: |q-x| per byte with
+//          __vabsdiffu4 and sums of squares with __dp4a, 8 lanes per row --
+//          exact integers, hence the reference's fp32 bits whenever
+//          dim * 255^2 <= 2^24.  Other queries: the sequential fold of the
+//          converted bytes (exact conversion, reference order).
+enum DistMode : int { kSeq = 0, kTeam = 1, kU8 = 2 };
 
 // Visited filter.
 //   kHash : exact set in shared memory; cleared and refilled from the beam when
@@ -48,7 +54,9 @@ enum ErrorFlag : unsigned int {
 // Everything a search launch needs, passed by value.
 struct SearchParams {
     // index (device pointers)
-    const float* vecs;          // [n][row_stride] f32, pad lanes zero
+    const float* vecs;          // [n][row_stride] f32, pad lanes zero (null in kU8)
+    const uint8_t* vecs8;       // [n][row_bytes] u8, pad bytes zero (kU8 only)
+    uint32_t row_bytes;         // dim rounded up to 16
     const uint32_t* adj;        // [n][degree] u32
     uint64_t n;
     uint32_t dim;
@@ -85,6 +93,7 @@ struct SearchParams {
     uint32_t stage_pitch;       // floats between staged rows (odd multiple of 4)
     // per-warp shared-memory carve-up (bytes)
     uint32_t smem_per_warp;
+    uint32_t off_q8;            // kU8: the query as packed u8 (row_bytes)
     uint32_t off_filter;
     uint32_t off_cids;
     uint32_t off_cdist;
@@ -121,9 +130,12 @@ cudaError_t launch_search_rabitq(const SearchParams& p, const LaunchShape& shape
 cudaError_t rabitq_grid_warps(const SearchParams& p, const LaunchShape& shape, int num_sms,
                               uint64_t& warps);
 
-// Entry point (bs_entry.cu): centroid-nearest row, reference arithmetic.
+// Entry point (bs_entry.cu): centroid-nearest row, reference arithmetic, over
+// f32 rows (vecs) or exact u8 rows (vecs8, row stride in bytes).
 cudaError_t compute_entry_point(const float* vecs, uint64_t n, uint32_t dim, uint32_t row_stride,
                                 uint32_t* d_result, float* d_scratch, cudaStream_t stream);
+cudaError_t compute_entry_point_u8(const uint8_t* vecs8, uint64_t n, uint32_t dim, uint32_t row_bytes,
+                                   uint32_t* d_result, float* d_scratch, cudaStream_t stream);
 size_t entry_point_scratch_bytes(uint64_t n, uint32_t dim);
 
 }  // namespace bsb

@@ -44,6 +44,7 @@ __global__ void __launch_bounds__(256) k_search_rabitq(const SearchParams p) {
     uint32_t* cids = reinterpret_cast<uint32_t*>(ws + p.off_cids);
     float* cdist = reinterpret_cast<float*>(ws + p.off_cdist);
     float* stage = reinterpret_cast<float*>(ws + p.off_stage);
+    uint32_t* q8 = reinterpret_cast<uint32_t*>(ws + p.off_q8);
     // rotated query (pdim floats) and bit-planes (kPlanes * wpp words) follow
     // the candidate arrays; the host reserves them in off_stage's front.
     float* qrot = reinterpret_cast<float*>(ws + p.off_stage - p.pdim * 4u - kPlanes * p.wpp * 4u);
@@ -71,8 +72,9 @@ __global__ void __launch_bounds__(256) k_search_rabitq(const SearchParams p) {
         for (uint32_t d = lane; d < p.row_stride; d += 32) qsm[d] = d < p.dim ? __ldg(q + d) : 0.0f;
         for (uint32_t i = lane; i < p.filter_words; i += 32) filt[i] = kNoNode;
         __syncwarp();
-        const bool team_ok = DM == kTeam && query_integer_exact(qsm, p.dim, p.team_qlo, p.team_qhi);
-        if (DM == kTeam && !team_ok && lane == 0) atomicAdd(&p.counters->team_fallbacks, 1u);
+        const bool team_ok = DM != kSeq && query_integer_exact(qsm, p.dim, p.team_qlo, p.team_qhi);
+        if (DM != kSeq && !team_ok && lane == 0) atomicAdd(&p.counters->team_fallbacks, 1u);
+        if (DM == kU8 && team_ok) pack_query_u8(qsm, p.dim, p.row_bytes, q8, lane);
 
         // ---- rotate + quantise (include/cpu_search_rabitq.hpp:34-57)
         for (uint32_t d = lane; d < pdim; d += 32)
@@ -117,7 +119,7 @@ __global__ void __launch_bounds__(256) k_search_rabitq(const SearchParams p) {
         __syncwarp();
 
         // ---- seed
-        score_rows<DM>(p, 1, cids, cdist, qsm, stage, lane, team_ok);
+        score_rows<DM>(p, 1, cids, cdist, qsm, q8, stage, lane, team_ok);
         uint64_t beam[RX];
 #pragma unroll
         for (int r = 0; r < RX; ++r) beam[r] = kEmptyKey;
@@ -165,24 +167,12 @@ __global__ void __launch_bounds__(256) k_search_rabitq(const SearchParams p) {
                 float e0 = 0.0f;
                 if (lane == 0) e0 = l2_seq(qsm, stage, p.dim);
                 exact = __shfl_sync(kFull, e0, 0);
-            } else if (team_ok) {
-                const float* src = p.vecs + static_cast<size_t>(cur) * p.row_stride;
-                float acc = 0.0f;
-                for (uint32_t d = lane * 4; d < p.row_stride; d += 128) {
-                    const float4 a = *reinterpret_cast<const float4*>(qsm + d);
-                    const float4 b = ldg_stream4(src + d);
-                    float t;
-                    t = a.x - b.x; acc = fmaf(t, t, acc);
-                    t = a.y - b.y; acc = fmaf(t, t, acc);
-                    t = a.z - b.z; acc = fmaf(t, t, acc);
-                    t = a.w - b.w; acc = fmaf(t, t, acc);
-                }
-                for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(kFull, acc, o);
-                exact = acc;
             } else {
-                float e0 = 0.0f;
-                if (lane == 0) e0 = l2_seq(qsm, p.vecs + static_cast<size_t>(cur) * p.row_stride, p.dim);
-                exact = __shfl_sync(kFull, e0, 0);
+                if (lane == 0) cids[0] = cur;
+                __syncwarp();
+                score_rows<DM>(p, 1, cids, cdist, qsm, q8, stage, lane, team_ok);
+                exact = cdist[0];
+                __syncwarp();   // cids/cdist are rewritten by the compaction below
             }
             ++D;
 
@@ -241,13 +231,17 @@ __global__ void __launch_bounds__(256) k_search_rabitq(const SearchParams p) {
             if (m) {
                 if (spilled) gfilled += m; else filled += m;
                 EST += m;
+                const uint64_t bound = beam_bound<RX>(beam, p.topk);
                 uint64_t cand[RY];
+                bool any = false;
 #pragma unroll
                 for (int r = 0; r < RY; ++r) {
                     const uint32_t s = static_cast<uint32_t>(r) * 32u + lane;
-                    cand[r] = s < m ? make_key(cdist[s], cids[s]) : kEmptyKey;
+                    const uint64_t k = s < m ? make_key(cdist[s], cids[s]) : kEmptyKey;
+                    cand[r] = k < bound ? k : kEmptyKey;
+                    any = any || cand[r] != kEmptyKey;
                 }
-                beam_merge<RX, RY>(beam, cand, lane, p.topk);
+                if (__any_sync(kFull, any)) beam_merge<RX, RY>(beam, cand, lane, p.topk);
             }
         }
 
@@ -261,7 +255,7 @@ __global__ void __launch_bounds__(256) k_search_rabitq(const SearchParams p) {
                 __syncwarp();
                 if (v) cids[lane] = key_id(beam[r]);
                 __syncwarp();
-                score_rows<DM>(p, cnt, cids, cdist, qsm, stage, lane, team_ok);
+                score_rows<DM>(p, cnt, cids, cdist, qsm, q8, stage, lane, team_ok);
                 if (v) beam[r] = make_key(cdist[lane], key_id(beam[r]));
                 rr += cnt;
             }
@@ -302,7 +296,9 @@ using KernelFn = void (*)(SearchParams);
 
 template <int RX, int RY>
 KernelFn pick_rq(int dm) {
-    return dm == kSeq ? k_search_rabitq<RX, RY, kSeq> : k_search_rabitq<RX, RY, kTeam>;
+    if (dm == kSeq) return k_search_rabitq<RX, RY, kSeq>;
+    if (dm == kU8) return k_search_rabitq<RX, RY, kU8>;
+    return k_search_rabitq<RX, RY, kTeam>;
 }
 
 KernelFn select_rq(int regx, int regy, int dm) {

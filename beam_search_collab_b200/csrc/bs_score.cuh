@@ -105,18 +105,143 @@ __device__ __forceinline__ void score_rows_team(const SearchParams& p, uint32_t 
     __syncwarp();
 }
 
+__device__ __forceinline__ uint4 ldg_stream_u4(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+// sum over the 4 bytes of (|a_b - x_b|)^2, added to acc (exact integers)
+__device__ __forceinline__ unsigned sq_absdiff4(unsigned a, unsigned x, unsigned acc) {
+    const unsigned d = __vabsdiffu4(a, x);
+    return __dp4a(d, d, acc);
+}
+
+// u8 rows and a query of integers in [0,255]: 4 teams of 8 lanes, up to 8
+// rows per team in flight (one 16-byte load per lane and row when the row is
+// at most 128 bytes), |q-x| per byte and dp4a sums of squares.  With
+// dim * 255^2 <= 2^24 (checked on the host) the integer sum is the
+// reference's fp32 result.
+__device__ __forceinline__ void score_rows_u8(const SearchParams& p, uint32_t m, const uint32_t* cids,
+                                              float* cdist, const uint32_t* q8, unsigned lane) {
+    const unsigned team = lane >> 3, tl = lane & 7u;
+    const unsigned char* qb = reinterpret_cast<const unsigned char*>(q8);
+    for (uint32_t s0 = 0; s0 < m; s0 += 32) {
+        unsigned acc[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] = 0u;
+        for (uint32_t off = tl * 16u; off < p.row_bytes; off += 128u) {
+            const uint4 q = *reinterpret_cast<const uint4*>(qb + off);
+            uint4 v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const uint32_t s = s0 + team + 4u * j;
+                v[j] = s < m ? ldg_stream_u4(p.vecs8 + static_cast<size_t>(cids[s]) * p.row_bytes + off)
+                             : make_uint4(0u, 0u, 0u, 0u);
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                acc[j] = sq_absdiff4(q.x, v[j].x, acc[j]);
+                acc[j] = sq_absdiff4(q.y, v[j].y, acc[j]);
+                acc[j] = sq_absdiff4(q.z, v[j].z, acc[j]);
+                acc[j] = sq_absdiff4(q.w, v[j].w, acc[j]);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            acc[j] += __shfl_xor_sync(kFull, acc[j], 4);
+            acc[j] += __shfl_xor_sync(kFull, acc[j], 2);
+            acc[j] += __shfl_xor_sync(kFull, acc[j], 1);
+        }
+        if (tl == 0) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const uint32_t s = s0 + team + 4u * j;
+                if (s < m) cdist[s] = static_cast<float>(acc[j]);
+            }
+        }
+    }
+    __syncwarp();
+}
+
+// u8 rows and any query: lane i folds row i in the reference order, each
+// byte converted to float exactly.
+__device__ __forceinline__ float l2_seq_u8(const float* __restrict__ q, const uint8_t* __restrict__ x,
+                                           uint32_t dim) {
+    float s = 0.0f;
+    uint32_t d = 0;
+    for (; d + 16 <= dim; d += 16) {
+        const uint4 w = ldg_stream_u4(x + d);
+        const unsigned words[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+            const float xv = static_cast<float>((words[k >> 2] >> (8 * (k & 3))) & 0xffu);
+            const float t = __fsub_rn(q[d + k], xv);
+            s = __fadd_rn(s, __fmul_rn(t, t));
+        }
+    }
+    for (; d < dim; ++d) {
+        const float t = __fsub_rn(q[d], static_cast<float>(x[d]));
+        s = __fadd_rn(s, __fmul_rn(t, t));
+    }
+    return s;
+}
+
+__device__ __forceinline__ void score_rows_u8_seq(const SearchParams& p, uint32_t m, const uint32_t* cids,
+                                                  float* cdist, const float* qsm, unsigned lane) {
+    for (uint32_t c0 = 0; c0 < m; c0 += 32) {
+        const uint32_t s = c0 + lane;
+        if (s < m) cdist[s] = l2_seq_u8(qsm, p.vecs8 + static_cast<size_t>(cids[s]) * p.row_bytes, p.dim);
+    }
+    __syncwarp();
+}
+
+// kU8: the query packed as bytes into q8 (row_bytes, zero pad), for a query
+// that passed query_integer_exact with a range inside [0,255].
+__device__ __forceinline__ void pack_query_u8(const float* qsm, uint32_t dim, uint32_t row_bytes,
+                                              uint32_t* q8, unsigned lane) {
+    for (uint32_t w = lane; w < row_bytes / 4u; w += 32) {
+        unsigned v = 0;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint32_t d = 4u * w + k;
+            const unsigned b = d < dim ? static_cast<unsigned>(qsm[d]) & 0xffu : 0u;
+            v |= b << (8 * k);
+        }
+        q8[w] = v;
+    }
+    __syncwarp();
+}
+
 // Dispatch on the compile-time distance mode and the per-query flag.
 template <int DM>
 __device__ __forceinline__ void score_rows(const SearchParams& p, uint32_t m, const uint32_t* cids,
-                                           float* cdist, const float* qsm, float* stage,
-                                           unsigned lane, bool team_ok) {
+                                           float* cdist, const float* qsm, const uint32_t* q8,
+                                           float* stage, unsigned lane, bool team_ok) {
     if (DM == kSeq) {
         score_rows_seq(p, m, cids, cdist, qsm, stage, lane);
-    } else if (team_ok) {
-        score_rows_team(p, m, cids, cdist, qsm, lane);
+    } else if (DM == kTeam) {
+        if (team_ok) score_rows_team(p, m, cids, cdist, qsm, lane);
+        else score_rows_seq_direct(p, m, cids, cdist, qsm, lane);
     } else {
-        score_rows_seq_direct(p, m, cids, cdist, qsm, lane);
+        if (team_ok) score_rows_u8(p, m, cids, cdist, q8, lane);
+        else score_rows_u8_seq(p, m, cids, cdist, qsm, lane);
     }
+}
+
+// Key of the beam's last admissible position (topk-1); kEmptyKey while the
+// beam is not full.  A candidate at or above it can never enter the beam.
+template <int RX>
+__device__ __forceinline__ uint64_t beam_bound(const uint64_t (&beam)[RX], uint32_t topk) {
+    const uint32_t pos = (topk < 32u * RX ? topk : 32u * RX) - 1u;
+    const int reg = static_cast<int>(pos >> 5);
+    uint64_t mine = kEmptyKey;
+#pragma unroll
+    for (int r = 0; r < RX; ++r)
+        if (r == reg) mine = beam[r];
+    return __shfl_sync(kFull, mine, static_cast<int>(pos & 31u));
 }
 
 }  // namespace dev

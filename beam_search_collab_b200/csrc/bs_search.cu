@@ -41,6 +41,7 @@ __global__ void __launch_bounds__(256) k_search_l2(const SearchParams p) {
     uint32_t* cids = reinterpret_cast<uint32_t*>(ws + p.off_cids);
     float* cdist = reinterpret_cast<float*>(ws + p.off_cdist);
     float* stage = reinterpret_cast<float*>(ws + p.off_stage);
+    uint32_t* q8 = reinterpret_cast<uint32_t*>(ws + p.off_q8);
 
     const uint32_t deg = p.degree;
     const uint32_t fmask = p.filter_slots - 1u;
@@ -60,11 +61,12 @@ __global__ void __launch_bounds__(256) k_search_l2(const SearchParams p) {
         for (uint32_t i = lane; i < p.filter_words; i += 32) filt[i] = (FM == kHash) ? kNoNode : 0u;
         if (lane == 0) cids[0] = p.entry;
         __syncwarp();
-        const bool team_ok = DM == kTeam && query_integer_exact(qsm, p.dim, p.team_qlo, p.team_qhi);
-        if (DM == kTeam && !team_ok && lane == 0) atomicAdd(&p.counters->team_fallbacks, 1u);
+        const bool team_ok = DM != kSeq && query_integer_exact(qsm, p.dim, p.team_qlo, p.team_qhi);
+        if (DM != kSeq && !team_ok && lane == 0) atomicAdd(&p.counters->team_fallbacks, 1u);
+        if (DM == kU8 && team_ok) pack_query_u8(qsm, p.dim, p.row_bytes, q8, lane);
 
         // seed: the entry point with its exact distance
-        score_rows<DM>(p, 1, cids, cdist, qsm, stage, lane, team_ok);
+        score_rows<DM>(p, 1, cids, cdist, qsm, q8, stage, lane, team_ok);
         uint64_t beam[RX];
 #pragma unroll
         for (int r = 0; r < RX; ++r) beam[r] = kEmptyKey;
@@ -149,14 +151,20 @@ __global__ void __launch_bounds__(256) k_search_l2(const SearchParams p) {
             if (m) {
                 filled += m;
                 D += m;
-                score_rows<DM>(p, m, cids, cdist, qsm, stage, lane, team_ok);
+                score_rows<DM>(p, m, cids, cdist, qsm, q8, stage, lane, team_ok);
+                // candidates at or above the full beam's last key cannot enter
+                // it; when none is left the merge is skipped (same result)
+                const uint64_t bound = beam_bound<RX>(beam, p.topk);
                 uint64_t cand[RY];
+                bool any = false;
 #pragma unroll
                 for (int r = 0; r < RY; ++r) {
                     const uint32_t s = static_cast<uint32_t>(r) * 32u + lane;
-                    cand[r] = s < m ? make_key(cdist[s], cids[s]) : kEmptyKey;
+                    const uint64_t k = s < m ? make_key(cdist[s], cids[s]) : kEmptyKey;
+                    cand[r] = k < bound ? k : kEmptyKey;
+                    any = any || cand[r] != kEmptyKey;
                 }
-                beam_merge<RX, RY>(beam, cand, lane, p.topk);
+                if (__any_sync(kFull, any)) beam_merge<RX, RY>(beam, cand, lane, p.topk);
             }
 
             if (FM == kBloom && p.reset_interval > 0 && (iter + 1) % p.reset_interval == 0) {
@@ -205,6 +213,7 @@ using KernelFn = void (*)(SearchParams);
 template <int RX, int RY>
 KernelFn pick_l2(int dm, int fm) {
     if (dm == kSeq) return fm == kHash ? k_search_l2<RX, RY, kSeq, kHash> : k_search_l2<RX, RY, kSeq, kBloom>;
+    if (dm == kU8) return fm == kHash ? k_search_l2<RX, RY, kU8, kHash> : k_search_l2<RX, RY, kU8, kBloom>;
     return fm == kHash ? k_search_l2<RX, RY, kTeam, kHash> : k_search_l2<RX, RY, kTeam, kBloom>;
 }
 
@@ -290,6 +299,8 @@ cudaError_t plan_search(SearchParams& p, LaunchShape& shape, size_t max_smem_opt
     const uint32_t cand = 32u * static_cast<uint32_t>(shape.regy);
 
     uint32_t off = align16(p.row_stride * 4u);
+    p.off_q8 = off;
+    if (shape.dmode == kU8) off = align16(off + p.row_bytes);
     p.off_filter = off;
     off = align16(off + p.filter_words * 4u);
     p.off_cids = off;

@@ -204,8 +204,10 @@ def run_ours(args, rank, world, local_rank):
     _, _, st = ix.search(q_dev, params)
     torch.cuda.synchronize()
     dim, deg = base.shape[1], edges.shape[1]
-    alg_bytes = (NQ_PER_GPU * 4 * dim + st.expansions * 4 * deg + st.distances * 4 * dim
-                 + NQ_PER_GPU * 4 * K)
+    # query read + adjacency rows + candidate rows as stored (u8 copy: 1 B/dim)
+    # + ids and distances written
+    alg_bytes = (NQ_PER_GPU * 4 * dim + st.expansions * 4 * deg + st.distances * st.row_bytes
+                 + NQ_PER_GPU * 8 * K)
 
     stream = torch.cuda.Stream(device=dev)
     flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
@@ -294,7 +296,8 @@ def run_ours(args, rank, world, local_rank):
             "recall@10": sweep[-1]["recall@10"] if chosen == sweep[-1]["topk_size"] else None,
             "recall_sweep": sweep,
             "entry_point": entry,
-            "distance_path": "integer-exact (8-lane teams)" if st.integer_exact else "sequential per lane",
+            "distance_path": ("integer-exact" if st.integer_exact else "sequential per lane")
+                             + f", stored row {st.row_bytes} B",
             "expansions_per_query": round(st.expansions / NQ_PER_GPU, 2),
             "distances_per_query": round(st.distances / NQ_PER_GPU, 2),
             "l2": "256 MiB write before every timed step (outside the timed window); index 640 MB > L2",

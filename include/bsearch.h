@@ -85,7 +85,7 @@ typedef struct bs_stats {
     uint32_t error_flags;     /* kernel-side error bits (0 = none)            */
     uint32_t entry_point;     /* entry node the search used                   */
     uint32_t integer_exact;   /* 1: integer-exact distance path was used       */
-    uint32_t reserved;
+    uint32_t row_bytes;       /* bytes per base row as stored on the device   */
 } bs_stats;
 
 /* Fills the reference defaults: mode "base", K 100, topk_size 256,

@@ -120,6 +120,30 @@ def test_integer_path_and_sequential_path_agree(indexes, monkeypatch):
     assert np.array_equal(d_t.view(np.uint32), d_s.view(np.uint32))
 
 
+def test_byte_storage_and_float_storage_agree(indexes, monkeypatch):
+    """i128 values are integers in [0,255]: the index keeps an exact u8 copy.
+    Forcing f32 rows must give the same ids and distance bits, for integer
+    queries, out-of-byte-range integer queries and fractional queries."""
+    g, ix_u8 = indexes["i128"]
+    monkeypatch.setenv("BSEARCH_STORAGE", "f32")
+    ix_f32 = B.Index.from_arrays(g.base, g.edges)
+    monkeypatch.delenv("BSEARCH_STORAGE")
+    try:
+        q_big = g.queries.copy()
+        q_big[::3, 5] = 300.0            # integer, outside the byte range
+        q_frac = g.queries.copy()
+        q_frac[1::2] += np.float32(0.5)
+        for q in (g.queries, q_big, q_frac):
+            a = ix_u8.search(q, mode="warp4", K=10, topk_size=64)
+            b = ix_f32.search(q, mode="warp4", K=10, topk_size=64)
+            ref = O.search(g.base, g.edges, q, K=10, topk_size=64, entry=g.entry)
+            assert np.array_equal(a[0], ref.ids) and np.array_equal(b[0], ref.ids)
+            assert np.array_equal(a[1].view(np.uint32), ref.dists.view(np.uint32))
+            assert np.array_equal(b[1].view(np.uint32), ref.dists.view(np.uint32))
+    finally:
+        ix_f32.close()
+
+
 def test_fractional_queries_leave_the_integer_path_and_stay_exact(indexes):
     g, ix = indexes["i128"]
     q = g.queries.copy()
