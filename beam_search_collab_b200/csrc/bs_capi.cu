@@ -22,7 +22,7 @@
 #include <thread>
 #include <vector>
 
-#include "../../include/bsearch.h"
+#include "bsearch.h"
 #include "bs_internal.h"
 #include "bs_io.hpp"
 
@@ -43,6 +43,10 @@ struct bs_index {
     uint32_t row_bytes = 0;
     uint8_t* d_vecs8 = nullptr;
     uint32_t* d_adj = nullptr;
+    // neighbourhood blocks (adjacency row + neighbour rows per node), built
+    // when they fit comfortably in device memory
+    unsigned char* d_nb = nullptr;
+    uint32_t nb_stride = 0, nb_adj_bytes = 0, nb_pitch = 0;
     bool int_exact = false;      // every base value an integer
     float min_val = 0.0f;        // range of the base values
     float max_val = 0.0f;
@@ -204,6 +208,66 @@ void pack_u8_rows(const float* v, uint64_t n, int32_t dim, uint32_t row_bytes, u
     for (auto& t : th) t.join();
 }
 
+// Neighbourhood blocks (one contiguous [adjacency | neighbour rows] block
+// per node, so that an expansion is one bulk copy).  Built when the blocks
+// take at most 40% of the device's free memory; BSEARCH_LAYOUT=gather turns
+// them off.  Row pitch: the stored row, grown to an odd number of 16-byte
+// units for f32 rows so that lanes reading one row each hit distinct banks.
+cudaError_t build_blocks(bs_index* ix) {
+    const char* env = std::getenv("BSEARCH_LAYOUT");
+    if (env && std::strcmp(env, "gather") == 0) return cudaSuccess;
+    uint32_t pitch;
+    if (ix->u8) {
+        pitch = ix->row_bytes;
+    } else {
+        pitch = ix->row_stride * 4u;
+        if ((pitch / 16u) % 2u == 0u) pitch += 16u;
+    }
+    const uint32_t adj_bytes = (static_cast<uint32_t>(ix->degree) * 4u + 15u) & ~15u;
+    const uint64_t stride = adj_bytes + static_cast<uint64_t>(ix->degree) * pitch;
+    if (stride > 64u * 1024u) return cudaSuccess;              // one block must fit a warp's shared memory
+    const uint64_t bytes = stride * ix->n;
+    size_t free_b = 0, total_b = 0;
+    if (cudaMemGetInfo(&free_b, &total_b) != cudaSuccess) { cudaGetLastError(); return cudaSuccess; }
+    if (bytes > free_b / 5u * 2u) return cudaSuccess;
+    if (cudaMalloc(&ix->d_nb, bytes) != cudaSuccess) {
+        cudaGetLastError();
+        ix->d_nb = nullptr;
+        return cudaSuccess;
+    }
+    ix->nb_stride = static_cast<uint32_t>(stride);
+    ix->nb_adj_bytes = adj_bytes;
+    ix->nb_pitch = pitch;
+    SearchParams p{};
+    p.vecs = ix->d_vecs;
+    p.vecs8 = ix->d_vecs8;
+    p.row_bytes = ix->row_bytes;
+    p.row_stride = ix->row_stride;
+    p.adj = ix->d_adj;
+    p.n = ix->n;
+    p.degree = static_cast<uint32_t>(ix->degree);
+    p.nb_stride = ix->nb_stride;
+    p.nb_adj_bytes = adj_bytes;
+    p.nb_pitch = pitch;
+    cudaError_t e = bsb::build_neighbourhood_blocks(p, ix->d_nb, nullptr);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    return e;
+}
+
+// Plans the launch; when a neighbourhood block per warp does not fit the
+// requested warps per block in shared memory, plans the gather layout.
+cudaError_t plan(const bs_index* ix, SearchParams& p, LaunchShape& shape, char* why, size_t why_len) {
+    SearchParams p0 = p;
+    const LaunchShape s0 = shape;
+    const cudaError_t e = bsb::plan_search(p, shape, ix->smem_optin, why, why_len);
+    if (e == cudaSuccess || p0.nb == nullptr) return e;
+    p0.nb = nullptr;
+    p0.nb_stride = p0.nb_adj_bytes = p0.nb_pitch = 0;
+    p = p0;
+    shape = s0;
+    return bsb::plan_search(p, shape, ix->smem_optin, why, why_len);
+}
+
 cudaError_t entry_kernels(const bs_index* ix, uint32_t* d_out, float* scratch, cudaStream_t stream) {
     return ix->u8 ? bsb::compute_entry_point_u8(ix->d_vecs8, ix->n, ix->dim, ix->row_bytes, d_out, scratch, stream)
                   : bsb::compute_entry_point(ix->d_vecs, ix->n, ix->dim, ix->row_stride, d_out, scratch, stream);
@@ -222,6 +286,12 @@ void fill_params(const bs_index* ix, const ModeInfo& mi, const bs_search_params*
     p.dim = static_cast<uint32_t>(ix->dim);
     p.row_stride = ix->row_stride;
     p.degree = static_cast<uint32_t>(ix->degree);
+    if (!mi.rabitq && ix->d_nb) {
+        p.nb = ix->d_nb;
+        p.nb_stride = ix->nb_stride;
+        p.nb_adj_bytes = ix->nb_adj_bytes;
+        p.nb_pitch = ix->nb_pitch;
+    }
     if (mi.rabitq) {
         p.codes = ix->d_codes;
         p.factors = ix->d_factors;
@@ -254,6 +324,7 @@ void free_index(bs_index* ix) {
     cudaFree(ix->d_vecs);
     cudaFree(ix->d_vecs8);
     cudaFree(ix->d_adj);
+    cudaFree(ix->d_nb);
     cudaFree(ix->d_codes);
     cudaFree(ix->d_factors);
     cudaFree(ix->d_signs);
@@ -362,6 +433,7 @@ BS_API bs_status bs_index_create(const bs_graph_desc* desc, int device, bs_index
     }
     if (e == cudaSuccess) e = cudaMemcpy(ix->d_adj, desc->edges, ebytes, cudaMemcpyHostToDevice);
     if (e != cudaSuccess) { free_index(ix); return cuda_fail(e, "index upload"); }
+    if ((e = build_blocks(ix)) != cudaSuccess) { free_index(ix); return cuda_fail(e, "neighbourhood blocks"); }
     // Per-call scratch comes from the device's stream-ordered pool: keep freed
     // blocks cached instead of returning them at every synchronisation.
     cudaMemPool_t pool;
@@ -490,7 +562,7 @@ BS_API bs_status bs_search(bs_index* ix, const bs_search_params* prm, const floa
     p.nq = nq;
     const bool use_team = p.team_qlo <= p.team_qhi;
     char why[256] = {0};
-    if (bsb::plan_search(p, shape, ix->smem_optin, why, sizeof(why)) != cudaSuccess)
+    if (plan(ix, p, shape, why, sizeof(why)) != cudaSuccess)
         return fail(BS_ERR_UNSUPPORTED, "%s", why);
 
     if (stats) {
@@ -498,6 +570,7 @@ BS_API bs_status bs_search(bs_index* ix, const bs_search_params* prm, const floa
         stats->entry_point = entry;
         stats->integer_exact = use_team ? 1u : 0u;
         stats->row_bytes = ix->u8 ? ix->row_bytes : ix->row_stride * 4u;
+        stats->block_bytes = p.nb ? p.nb_stride : 0u;
     }
     if (nq == 0) return BS_OK;
 
@@ -538,6 +611,7 @@ BS_API bs_status bs_search(bs_index* ix, const bs_search_params* prm, const floa
     if (e != cudaSuccess) { release(); return cuda_fail(e, "query upload"); }
 
     e = mi.rabitq ? bsb::launch_search_rabitq(p, shape, ix->num_sms, stream)
+        : p.nb    ? bsb::launch_search_nb(p, shape, ix->num_sms, stream)
                   : bsb::launch_search(p, shape, ix->num_sms, stream);
     if (e != cudaSuccess) { release(); return cuda_fail(e, "search launch"); }
 
@@ -680,14 +754,15 @@ BS_API bs_status bs_search_no_alloc(bs_index* ix, const bs_search_params* prm, c
     p.out_dists = dists;
     p.counters = reinterpret_cast<DevCounters*>(scratch);
     char why[256] = {0};
-    if (bsb::plan_search(p, shape, ix->smem_optin, why, sizeof(why)) != cudaSuccess)
+    if (plan(ix, p, shape, why, sizeof(why)) != cudaSuccess)
         return fail(BS_ERR_UNSUPPORTED, "%s", why);
 
     // the array keeps the previous call's contents: the work queue and the
     // counters must start from zero
     cudaError_t e = cudaMemsetAsync(scratch, 0, sizeof(DevCounters), stream);
     if (e != cudaSuccess) return cuda_fail(e, "fixed scratch reset");
-    e = bsb::launch_search(p, shape, ix->num_sms, stream);
+    e = p.nb ? bsb::launch_search_nb(p, shape, ix->num_sms, stream)
+             : bsb::launch_search(p, shape, ix->num_sms, stream);
     if (e != cudaSuccess) return cuda_fail(e, "search launch");
     return BS_OK;
 }

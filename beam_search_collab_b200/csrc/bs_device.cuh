@@ -129,6 +129,63 @@ __device__ __forceinline__ void beam_merge(uint64_t (&beam)[RX], uint64_t (&cand
         if (static_cast<unsigned>(r) * 32u + lane >= topk) beam[r] = kEmptyKey;
 }
 
+// Insert one key c into the ascending beam (kept to `topk` entries): every
+// entry above c moves up one position.  A key at or past position topk is
+// dropped, so inserting a key that no longer fits leaves the beam unchanged.
+template <int RX>
+__device__ __forceinline__ void beam_insert1(uint64_t (&beam)[RX], unsigned lane, uint64_t c,
+                                             unsigned topk) {
+    unsigned pos = 0;
+#pragma unroll
+    for (int r = 0; r < RX; ++r) pos += __popc(__ballot_sync(kFull, beam[r] < c));
+    uint64_t up[RX], last[RX];
+#pragma unroll
+    for (int r = 0; r < RX; ++r) {
+        up[r] = __shfl_up_sync(kFull, beam[r], 1);
+        last[r] = __shfl_sync(kFull, beam[r], 31);
+    }
+#pragma unroll
+    for (int r = 0; r < RX; ++r) {
+        const unsigned p = static_cast<unsigned>(r) * 32u + lane;
+        const uint64_t prev = lane ? up[r] : (r > 0 ? last[r > 0 ? r - 1 : 0] : kEmptyKey);
+        const uint64_t nv = p > pos ? prev : (p == pos ? c : beam[r]);
+        beam[r] = p >= topk ? kEmptyKey : nv;
+    }
+}
+
+// Merge `count` candidate keys, already compacted into ckeys[0..count) in
+// shared memory, into the beam.  One or two keys are shifted in directly;
+// otherwise the keys are sorted with the smallest bitonic network that holds
+// them (8, 16, 32 or 32*RY; the empty slots hold kEmptyKey, the largest key,
+// so the full candidate array is sorted) and merged as in beam_merge.
+template <int RX, int RY>
+__device__ __forceinline__ void beam_merge_compact(uint64_t (&beam)[RX], const uint64_t* ckeys,
+                                                   unsigned count, unsigned lane, unsigned topk) {
+    if (count <= 2) {
+        for (unsigned j = 0; j < count; ++j) beam_insert1<RX>(beam, lane, ckeys[j], topk);
+        return;
+    }
+    uint64_t cand[RY];
+#pragma unroll
+    for (int r = 0; r < RY; ++r) {
+        const unsigned s = static_cast<unsigned>(r) * 32u + lane;
+        cand[r] = s < count ? ckeys[s] : kEmptyKey;
+    }
+    if (count <= 8) sort_stages<RY, 8>(cand, lane);
+    else if (count <= 16) sort_stages<RY, 16>(cand, lane);
+    else if (count <= 32) sort_stages<RY, 32>(cand, lane);
+    else sort_stages<RY, 32u * RY>(cand, lane);
+#pragma unroll
+    for (int r = RX - RY; r < RX; ++r) {
+        const uint64_t c = __shfl_xor_sync(kFull, cand[RX - 1 - r], 31);
+        beam[r] = kmin(beam[r], c);
+    }
+    merge_asc<RX>(beam, lane);
+#pragma unroll
+    for (int r = 0; r < RX; ++r)
+        if (static_cast<unsigned>(r) * 32u + lane >= topk) beam[r] = kEmptyKey;
+}
+
 // Smallest unexpanded entry: mark it and return its node id.  Branch-free
 // over the registers so the beam stays in registers.
 template <int RX>
@@ -169,9 +226,14 @@ __device__ __forceinline__ int hash_insert(uint32_t* tab, uint32_t mask, uint32_
                                            uint32_t key, unsigned& err) {
     uint32_t h = hash_slot(key, shift);
     for (uint32_t i = 0; i <= mask; ++i) {
-        const uint32_t old = atomicCAS(&tab[h], kNoNode, key);
-        if (old == kNoNode) return 1;
-        if (old == key) return 0;
+        // plain read first: a key already present (the common case for
+        // neighbours of neighbours) or an occupied slot needs no atomic
+        uint32_t v = tab[h];
+        if (v == kNoNode) {
+            v = atomicCAS(&tab[h], kNoNode, key);
+            if (v == kNoNode) return 1;
+        }
+        if (v == key) return 0;
         h = (h + 1) & mask;
     }
     err |= 1u;   // table full: cannot happen with the host's load bound

@@ -49,6 +49,7 @@ struct DevCounters {
 enum ErrorFlag : unsigned int {
     kErrProbeBound = 1u,     // a visited-table probe ran the whole table
     kErrSpillFull = 2u,      // a query overflowed its RaBitQ spill table
+    kErrWaitTimeout = 4u,    // a bulk-copy wait hit its iteration bound
 };
 
 // Everything a search launch needs, passed by value.
@@ -58,6 +59,16 @@ struct SearchParams {
     const uint8_t* vecs8;       // [n][row_bytes] u8, pad bytes zero (kU8 only)
     uint32_t row_bytes;         // dim rounded up to 16
     const uint32_t* adj;        // [n][degree] u32
+    // neighbourhood blocks (null: gather layout): per node, its adjacency row
+    // (nb_adj_bytes) then the rows of its degree neighbours, nb_pitch bytes
+    // apart; nb_stride bytes per node, all multiples of 16
+    const unsigned char* nb;
+    uint32_t nb_stride;
+    uint32_t nb_adj_bytes;
+    uint32_t nb_pitch;
+    uint32_t off_block;         // per-warp copy of one block
+    uint32_t off_mbar;          // per-warp mbarrier (8 bytes)
+    uint32_t off_cpos;          // block positions of the compacted candidates
     uint64_t n;
     uint32_t dim;
     uint32_t row_stride;        // floats per stored row (dim rounded up to 4)
@@ -97,6 +108,7 @@ struct SearchParams {
     uint32_t off_filter;
     uint32_t off_cids;
     uint32_t off_cdist;
+    uint32_t off_keys;          // compacted candidate keys for the merge (u64)
     uint32_t off_stage;
     uint32_t filter_words;      // u32 words of the filter table
     // outputs
@@ -126,6 +138,12 @@ cudaError_t launch_search(const SearchParams& p, const LaunchShape& shape, int n
                           cudaStream_t stream);
 cudaError_t launch_search_rabitq(const SearchParams& p, const LaunchShape& shape, int num_sms,
                                  cudaStream_t stream);
+// Neighbourhood-block variant of launch_search (p.nb set; bs_search_nb.cu).
+cudaError_t launch_search_nb(const SearchParams& p, const LaunchShape& shape, int num_sms,
+                             cudaStream_t stream);
+// Builds the neighbourhood blocks from the gather layout (bs_search_nb.cu).
+cudaError_t build_neighbourhood_blocks(const SearchParams& p, unsigned char* out, cudaStream_t stream);
+
 // Resident warps of the RaBitQ launch for `shape` (sizes the spill tables).
 cudaError_t rabitq_grid_warps(const SearchParams& p, const LaunchShape& shape, int num_sms,
                               uint64_t& warps);

@@ -45,6 +45,7 @@ __global__ void __launch_bounds__(256) k_search_rabitq(const SearchParams p) {
     float* cdist = reinterpret_cast<float*>(ws + p.off_cdist);
     float* stage = reinterpret_cast<float*>(ws + p.off_stage);
     uint32_t* q8 = reinterpret_cast<uint32_t*>(ws + p.off_q8);
+    uint64_t* ckeys = reinterpret_cast<uint64_t*>(ws + p.off_keys);
     // rotated query (pdim floats) and bit-planes (kPlanes * wpp words) follow
     // the candidate arrays; the host reserves them in off_stage's front.
     float* qrot = reinterpret_cast<float*>(ws + p.off_stage - p.pdim * 4u - kPlanes * p.wpp * 4u);
@@ -232,16 +233,20 @@ __global__ void __launch_bounds__(256) k_search_rabitq(const SearchParams p) {
                 if (spilled) gfilled += m; else filled += m;
                 EST += m;
                 const uint64_t bound = beam_bound<RX>(beam, p.topk);
-                uint64_t cand[RY];
-                bool any = false;
+                unsigned cnt = 0;
 #pragma unroll
                 for (int r = 0; r < RY; ++r) {
                     const uint32_t s = static_cast<uint32_t>(r) * 32u + lane;
                     const uint64_t k = s < m ? make_key(cdist[s], cids[s]) : kEmptyKey;
-                    cand[r] = k < bound ? k : kEmptyKey;
-                    any = any || cand[r] != kEmptyKey;
+                    const bool keep = k < bound;
+                    const unsigned b = __ballot_sync(kFull, keep);
+                    if (keep) ckeys[cnt + __popc(b & lt_mask)] = k;
+                    cnt += __popc(b);
                 }
-                if (__any_sync(kFull, any)) beam_merge<RX, RY>(beam, cand, lane, p.topk);
+                if (cnt) {
+                    __syncwarp();
+                    beam_merge_compact<RX, RY>(beam, ckeys, cnt, lane, p.topk);
+                }
             }
         }
 

@@ -113,57 +113,70 @@ __device__ __forceinline__ uint4 ldg_stream_u4(const void* p) {
     return v;
 }
 
-// sum over the 4 bytes of (|a_b - x_b|)^2, added to acc (exact integers)
-__device__ __forceinline__ unsigned sq_absdiff4(unsigned a, unsigned x, unsigned acc) {
-    const unsigned d = __vabsdiffu4(a, x);
-    return __dp4a(d, d, acc);
-}
-
 // u8 rows and a query of integers in [0,255]: 4 teams of 8 lanes, up to 8
 // rows per team in flight (one 16-byte load per lane and row when the row is
-// at most 128 bytes), |q-x| per byte and dp4a sums of squares.  With
-// dim * 255^2 <= 2^24 (checked on the host) the integer sum is the
-// reference's fp32 result.
-__device__ __forceinline__ void score_rows_u8(const SearchParams& p, uint32_t m, const uint32_t* cids,
-                                              float* cdist, const uint32_t* q8, unsigned lane) {
+// at most 128 bytes) and dp4a integer dot products.  With dim * 255^2 <= 2^24
+// (checked on the host) the integer sum is the reference's fp32 result.
+// sum(q - x)^2 = sum q^2 + sum x^2 - 2 sum q*x over the bytes, each term an
+// exact integer: two dp4a per 4 dimensions.  qq = sum q^2 of the query.
+template <int SLOTS>
+__device__ __forceinline__ void score_rows_u8_slots(const SearchParams& p, uint32_t m, const uint32_t* cids,
+                                                    float* cdist, const uint32_t* q8, unsigned qq,
+                                                    unsigned lane) {
     const unsigned team = lane >> 3, tl = lane & 7u;
     const unsigned char* qb = reinterpret_cast<const unsigned char*>(q8);
-    for (uint32_t s0 = 0; s0 < m; s0 += 32) {
-        unsigned acc[8];
+    for (uint32_t s0 = 0; s0 < m; s0 += 4u * SLOTS) {
+        unsigned xx[SLOTS], qx[SLOTS];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[j] = 0u;
+        for (int j = 0; j < SLOTS; ++j) { xx[j] = 0u; qx[j] = 0u; }
         for (uint32_t off = tl * 16u; off < p.row_bytes; off += 128u) {
             const uint4 q = *reinterpret_cast<const uint4*>(qb + off);
-            uint4 v[8];
+            uint4 v[SLOTS];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
+            for (int j = 0; j < SLOTS; ++j) {
                 const uint32_t s = s0 + team + 4u * j;
                 v[j] = s < m ? ldg_stream_u4(p.vecs8 + static_cast<size_t>(cids[s]) * p.row_bytes + off)
                              : make_uint4(0u, 0u, 0u, 0u);
             }
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                acc[j] = sq_absdiff4(q.x, v[j].x, acc[j]);
-                acc[j] = sq_absdiff4(q.y, v[j].y, acc[j]);
-                acc[j] = sq_absdiff4(q.z, v[j].z, acc[j]);
-                acc[j] = sq_absdiff4(q.w, v[j].w, acc[j]);
+            for (int j = 0; j < SLOTS; ++j) {
+                xx[j] = __dp4a(v[j].x, v[j].x, xx[j]);
+                qx[j] = __dp4a(q.x, v[j].x, qx[j]);
+                xx[j] = __dp4a(v[j].y, v[j].y, xx[j]);
+                qx[j] = __dp4a(q.y, v[j].y, qx[j]);
+                xx[j] = __dp4a(v[j].z, v[j].z, xx[j]);
+                qx[j] = __dp4a(q.z, v[j].z, qx[j]);
+                xx[j] = __dp4a(v[j].w, v[j].w, xx[j]);
+                qx[j] = __dp4a(q.w, v[j].w, qx[j]);
             }
         }
+        unsigned acc[SLOTS];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
+        for (int j = 0; j < SLOTS; ++j) acc[j] = xx[j] - 2u * qx[j];   // mod 2^32; qq added below
+#pragma unroll
+        for (int j = 0; j < SLOTS; ++j) {
             acc[j] += __shfl_xor_sync(kFull, acc[j], 4);
             acc[j] += __shfl_xor_sync(kFull, acc[j], 2);
             acc[j] += __shfl_xor_sync(kFull, acc[j], 1);
         }
         if (tl == 0) {
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
+            for (int j = 0; j < SLOTS; ++j) {
                 const uint32_t s = s0 + team + 4u * j;
-                if (s < m) cdist[s] = static_cast<float>(acc[j]);
+                if (s < m) cdist[s] = static_cast<float>(acc[j] + qq);
             }
         }
     }
     __syncwarp();
+}
+
+// up to 1, 4 or 8 rows per team (rows in flight per lane) by list length
+__device__ __forceinline__ void score_rows_u8(const SearchParams& p, uint32_t m, const uint32_t* cids,
+                                              float* cdist, const uint32_t* q8, unsigned lane) {
+    const unsigned qq = q8[p.row_bytes / 4u];   // sum of q^2, stored after the packed bytes
+    if (m <= 4) score_rows_u8_slots<1>(p, m, cids, cdist, q8, qq, lane);
+    else if (m <= 16) score_rows_u8_slots<4>(p, m, cids, cdist, q8, qq, lane);
+    else score_rows_u8_slots<8>(p, m, cids, cdist, q8, qq, lane);
 }
 
 // u8 rows and any query: lane i folds row i in the reference order, each
@@ -198,10 +211,12 @@ __device__ __forceinline__ void score_rows_u8_seq(const SearchParams& p, uint32_
     __syncwarp();
 }
 
-// kU8: the query packed as bytes into q8 (row_bytes, zero pad), for a query
-// that passed query_integer_exact with a range inside [0,255].
+// kU8: the query packed as bytes into q8 (row_bytes, zero pad) followed by
+// the word sum q^2, for a query that passed query_integer_exact with a range
+// inside [0,255].
 __device__ __forceinline__ void pack_query_u8(const float* qsm, uint32_t dim, uint32_t row_bytes,
                                               uint32_t* q8, unsigned lane) {
+    unsigned qq = 0;
     for (uint32_t w = lane; w < row_bytes / 4u; w += 32) {
         unsigned v = 0;
 #pragma unroll
@@ -211,7 +226,10 @@ __device__ __forceinline__ void pack_query_u8(const float* qsm, uint32_t dim, ui
             v |= b << (8 * k);
         }
         q8[w] = v;
+        qq = __dp4a(v, v, qq);
     }
+    for (int o = 16; o > 0; o >>= 1) qq += __shfl_xor_sync(kFull, qq, o);
+    if (lane == 0) q8[row_bytes / 4u] = qq;
     __syncwarp();
 }
 

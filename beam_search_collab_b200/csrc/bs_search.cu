@@ -42,6 +42,7 @@ __global__ void __launch_bounds__(256) k_search_l2(const SearchParams p) {
     float* cdist = reinterpret_cast<float*>(ws + p.off_cdist);
     float* stage = reinterpret_cast<float*>(ws + p.off_stage);
     uint32_t* q8 = reinterpret_cast<uint32_t*>(ws + p.off_q8);
+    uint64_t* ckeys = reinterpret_cast<uint64_t*>(ws + p.off_keys);
 
     const uint32_t deg = p.degree;
     const uint32_t fmask = p.filter_slots - 1u;
@@ -153,18 +154,22 @@ __global__ void __launch_bounds__(256) k_search_l2(const SearchParams p) {
                 D += m;
                 score_rows<DM>(p, m, cids, cdist, qsm, q8, stage, lane, team_ok);
                 // candidates at or above the full beam's last key cannot enter
-                // it; when none is left the merge is skipped (same result)
+                // it; the others are compacted and merged (none: no merge)
                 const uint64_t bound = beam_bound<RX>(beam, p.topk);
-                uint64_t cand[RY];
-                bool any = false;
+                unsigned cnt = 0;
 #pragma unroll
                 for (int r = 0; r < RY; ++r) {
                     const uint32_t s = static_cast<uint32_t>(r) * 32u + lane;
                     const uint64_t k = s < m ? make_key(cdist[s], cids[s]) : kEmptyKey;
-                    cand[r] = k < bound ? k : kEmptyKey;
-                    any = any || cand[r] != kEmptyKey;
+                    const bool keep = k < bound;
+                    const unsigned b = __ballot_sync(kFull, keep);
+                    if (keep) ckeys[cnt + __popc(b & lt_mask)] = k;
+                    cnt += __popc(b);
                 }
-                if (__any_sync(kFull, any)) beam_merge<RX, RY>(beam, cand, lane, p.topk);
+                if (cnt) {
+                    __syncwarp();
+                    beam_merge_compact<RX, RY>(beam, ckeys, cnt, lane, p.topk);
+                }
             }
 
             if (FM == kBloom && p.reset_interval > 0 && (iter + 1) % p.reset_interval == 0) {
@@ -280,7 +285,11 @@ cudaError_t plan_search(SearchParams& p, LaunchShape& shape, size_t max_smem_opt
     } else if (shape.fmode == kHash) {
         // Room for the beam plus several rows between resets, at <= 3/4 load.
         const uint64_t need = (static_cast<uint64_t>(p.topk) + 4ull * p.degree) * 4ull / 3ull + 1;
-        const uint32_t slots = pow2_at_least(p.filter_slots > need ? p.filter_slots : need);
+        // With neighbourhood blocks a forgotten node costs only a distance
+        // over rows already in shared memory, so the table is sized to the
+        // beam (more resets, more resident warps) instead of filter_capacity.
+        const uint64_t want = p.nb != nullptr ? need : (p.filter_slots > need ? p.filter_slots : need);
+        const uint32_t slots = pow2_at_least(want);
         p.filter_slots = slots < 64 ? 64 : slots;
         p.filter_limit = p.filter_slots / 4u * 3u;
         p.filter_words = p.filter_slots;
@@ -300,13 +309,15 @@ cudaError_t plan_search(SearchParams& p, LaunchShape& shape, size_t max_smem_opt
 
     uint32_t off = align16(p.row_stride * 4u);
     p.off_q8 = off;
-    if (shape.dmode == kU8) off = align16(off + p.row_bytes);
+    if (shape.dmode == kU8) off = align16(off + p.row_bytes + 4u);   // bytes + sum q^2
     p.off_filter = off;
     off = align16(off + p.filter_words * 4u);
     p.off_cids = off;
     off = align16(off + cand * 4u);
     p.off_cdist = off;
     off = align16(off + cand * 4u);
+    p.off_keys = off;
+    off = align16(off + cand * 8u);
     if (p.codes != nullptr) {
         // RaBitQ: rotated query and the 7 bit-planes sit right below the
         // staging area (the kernel addresses them from off_stage down).
@@ -314,7 +325,17 @@ cudaError_t plan_search(SearchParams& p, LaunchShape& shape, size_t max_smem_opt
         off = align16(off + p.pdim * 4u + 7u * p.wpp * 4u);
     }
     p.off_stage = off;
-    if (shape.dmode == kSeq) {
+    if (p.nb != nullptr && p.codes == nullptr) {
+        // neighbourhood blocks: candidate positions, the mbarrier and one
+        // block copy replace the staging area
+        p.off_cpos = off;
+        off = align16(off + cand * 4u);
+        p.off_mbar = off;
+        off = align16(off + 8u);
+        p.off_block = off;
+        off = align16(off + p.nb_stride);
+        p.stage_rows = 0;
+    } else if (shape.dmode == kSeq) {
         const uint32_t row_bytes = p.stage_pitch * 4u;
         // up to 32 rows per round, within ~48 KB per warp
         uint32_t rows = (48u * 1024u) / row_bytes;

@@ -1,0 +1,464 @@
+// bs_search_nb.cu -- the exact L2 beam search (modes base, warp1..8,
+// bwarp1..8) over neighbourhood blocks.
+//
+// Same semantics as bs_search.cu (the reference CPU search,
+// include/cpu_search_base.hpp:22-82); only the memory path differs.  The
+// gather layout needs two dependent round trips per expansion -- the node's
+// adjacency row, then the rows of its unvisited neighbours.  Here every node
+// owns one contiguous block in HBM:
+//
+//     [ adjacency row (degree u32, padded to 16 B) | row of neighbour 0 | ... ]
+//
+// so an expansion is ONE bulk copy (cp.async.bulk global->shared, completion
+// counted on a per-warp mbarrier) of the expanded node's block, after which
+// the visited filter, the distances and the merge all read shared memory.
+// The blocks trade capacity for latency (C2: 4.2 KB per node, 4.2 GB for
+// 1M nodes); the host builds them only when they fit the device comfortably.
+#include <cfloat>
+#include <cstdio>
+
+#include "bs_device.cuh"
+#include "bs_internal.h"
+#include "bs_score.cuh"
+
+namespace bsb {
+
+using namespace dev;
+
+namespace {
+
+// ------------------------------------------------------- bulk copy + mbarrier
+
+__device__ __forceinline__ unsigned smem_u32(const void* p) {
+    return static_cast<unsigned>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* mbar) {
+    asm volatile("mbarrier.init.shared.b64 [%0], 1;\n" ::"r"(smem_u32(mbar)) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+}
+
+// One lane: announce `bytes` of transaction and start the copy.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, unsigned bytes, uint64_t* mbar) {
+    // the warp's earlier generic-proxy reads of dst are ordered before the
+    // asynchronous write that follows
+    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+    asm volatile("mbarrier.arrive.expect_tx.shared.b64 _, [%0], %1;\n" ::"r"(smem_u32(mbar)), "r"(bytes)
+                 : "memory");
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(mbar))
+        : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* mbar, unsigned phase) {
+    unsigned ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(mbar)), "r"(phase)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait: every lane polls at most kMaxPolls times (each try_wait may
+// itself suspend for a while); the warp agrees on the outcome.
+constexpr unsigned kMaxPolls = 1u << 22;
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* mbar, unsigned phase) {
+    bool done = false;
+    for (unsigned i = 0; i < kMaxPolls && !done; ++i) done = mbar_try_wait(mbar, phase);
+    return __all_sync(kFull, done);
+}
+
+// ------------------------------------------------------------- scoring
+
+// Distances of the compacted candidates s < m whose rows sit in the block at
+// positions cpos[s].  Same arithmetic as the gather scorers in bs_score.cuh.
+// Rows come from shared memory, so a few per team in flight suffice (and keep
+// the register count, hence the resident warps, up).
+constexpr int kSlots = 4;
+
+template <int DM>
+__device__ __forceinline__ void score_block(const SearchParams& p, uint32_t m, const uint32_t* cpos,
+                                            const unsigned char* rows, float* cdist, const float* qsm,
+                                            const uint32_t* q8, unsigned lane, bool team_ok) {
+    if (DM == kU8 && team_ok) {
+        const unsigned team = lane >> 3, tl = lane & 7u;
+        const unsigned char* qb = reinterpret_cast<const unsigned char*>(q8);
+        const unsigned qq = q8[p.row_bytes / 4u];
+        for (uint32_t s0 = 0; s0 < m; s0 += 4u * kSlots) {
+            unsigned xx[kSlots], qx[kSlots];
+#pragma unroll
+            for (int j = 0; j < kSlots; ++j) { xx[j] = 0u; qx[j] = 0u; }
+            for (uint32_t off = tl * 16u; off < p.row_bytes; off += 128u) {
+                const uint4 q = *reinterpret_cast<const uint4*>(qb + off);
+#pragma unroll
+                for (int j = 0; j < kSlots; ++j) {
+                    const uint32_t s = s0 + team + 4u * j;
+                    if (s < m) {
+                        const uint4 v = *reinterpret_cast<const uint4*>(rows + cpos[s] * p.nb_pitch + off);
+                        xx[j] = __dp4a(v.x, v.x, xx[j]); qx[j] = __dp4a(q.x, v.x, qx[j]);
+                        xx[j] = __dp4a(v.y, v.y, xx[j]); qx[j] = __dp4a(q.y, v.y, qx[j]);
+                        xx[j] = __dp4a(v.z, v.z, xx[j]); qx[j] = __dp4a(q.z, v.z, qx[j]);
+                        xx[j] = __dp4a(v.w, v.w, xx[j]); qx[j] = __dp4a(q.w, v.w, qx[j]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < kSlots; ++j) {
+                unsigned a = xx[j] - 2u * qx[j];
+                a += __shfl_xor_sync(kFull, a, 4);
+                a += __shfl_xor_sync(kFull, a, 2);
+                a += __shfl_xor_sync(kFull, a, 1);
+                const uint32_t s = s0 + team + 4u * j;
+                if (tl == 0 && s < m) cdist[s] = static_cast<float>(a + qq);
+            }
+        }
+    } else if (DM == kTeam && team_ok) {
+        const unsigned team = lane >> 3, tl = lane & 7u;
+        for (uint32_t s0 = 0; s0 < m; s0 += 4u * kSlots) {
+            float acc[kSlots];
+#pragma unroll
+            for (int j = 0; j < kSlots; ++j) acc[j] = 0.0f;
+            for (uint32_t d = tl * 4u; d < p.row_stride; d += 32u) {
+                const float4 qv = *reinterpret_cast<const float4*>(qsm + d);
+#pragma unroll
+                for (int j = 0; j < kSlots; ++j) {
+                    const uint32_t s = s0 + team + 4u * j;
+                    if (s < m) {
+                        const float4 v = *reinterpret_cast<const float4*>(rows + cpos[s] * p.nb_pitch + 4u * d);
+                        float t;
+                        t = qv.x - v.x; acc[j] = fmaf(t, t, acc[j]);
+                        t = qv.y - v.y; acc[j] = fmaf(t, t, acc[j]);
+                        t = qv.z - v.z; acc[j] = fmaf(t, t, acc[j]);
+                        t = qv.w - v.w; acc[j] = fmaf(t, t, acc[j]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < kSlots; ++j) {
+                float a = acc[j];
+                a += __shfl_xor_sync(kFull, a, 4);
+                a += __shfl_xor_sync(kFull, a, 2);
+                a += __shfl_xor_sync(kFull, a, 1);
+                const uint32_t s = s0 + team + 4u * j;
+                if (tl == 0 && s < m) cdist[s] = a;
+            }
+        }
+    } else {
+        // the reference's sequential fold, one lane per row
+        for (uint32_t c0 = 0; c0 < m; c0 += 32) {
+            const uint32_t s = c0 + lane;
+            if (s < m) {
+                const unsigned char* r = rows + cpos[s] * p.nb_pitch;
+                float v;
+                if (DM == kU8) {
+                    float acc = 0.0f;
+                    for (uint32_t d = 0; d < p.dim; ++d) {
+                        const float t = __fsub_rn(qsm[d], static_cast<float>(r[d]));
+                        acc = __fadd_rn(acc, __fmul_rn(t, t));
+                    }
+                    v = acc;
+                } else {
+                    v = l2_seq(qsm, reinterpret_cast<const float*>(r), p.dim);
+                }
+                cdist[s] = v;
+            }
+        }
+    }
+    __syncwarp();
+}
+
+// Exact distance of one node straight from the gather layout (the entry).
+template <int DM>
+__device__ __forceinline__ void score_direct(const SearchParams& p, uint32_t m, const uint32_t* cids,
+                                             float* cdist, const float* qsm, const uint32_t* q8,
+                                             unsigned lane, bool team_ok) {
+    if (DM == kU8) {
+        if (team_ok) score_rows_u8(p, m, cids, cdist, q8, lane);
+        else score_rows_u8_seq(p, m, cids, cdist, qsm, lane);
+    } else if (DM == kTeam && team_ok) {
+        score_rows_team(p, m, cids, cdist, qsm, lane);
+    } else {
+        score_rows_seq_direct(p, m, cids, cdist, qsm, lane);
+    }
+}
+
+template <int RX, int RY, int DM, int FM>
+__global__ void __launch_bounds__(256) k_search_nb(const SearchParams p) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const unsigned lane = threadIdx.x & 31u;
+    unsigned char* ws = smem_raw + static_cast<size_t>(threadIdx.x >> 5) * p.smem_per_warp;
+    float* qsm = reinterpret_cast<float*>(ws);
+    uint32_t* q8 = reinterpret_cast<uint32_t*>(ws + p.off_q8);
+    uint32_t* filt = reinterpret_cast<uint32_t*>(ws + p.off_filter);
+    uint32_t* cids = reinterpret_cast<uint32_t*>(ws + p.off_cids);
+    float* cdist = reinterpret_cast<float*>(ws + p.off_cdist);
+    uint64_t* ckeys = reinterpret_cast<uint64_t*>(ws + p.off_keys);
+    uint32_t* cpos = reinterpret_cast<uint32_t*>(ws + p.off_cpos);
+    uint64_t* mbar = reinterpret_cast<uint64_t*>(ws + p.off_mbar);
+    unsigned char* blk = ws + p.off_block;
+    const uint32_t* blk_adj = reinterpret_cast<const uint32_t*>(blk);
+    const unsigned char* blk_rows = blk + p.nb_adj_bytes;
+
+    const uint32_t deg = p.degree;
+    const uint32_t fmask = p.filter_slots - 1u;
+    const uint32_t fshift = 32u - static_cast<uint32_t>(__popc(fmask));
+    const unsigned lt_mask = (1u << lane) - 1u;
+    unsigned err = 0;
+    unsigned phase = 0;
+    if (lane == 0) mbar_init(mbar);
+    __syncwarp();
+
+    for (;;) {
+        unsigned qi = 0;
+        if (lane == 0) qi = atomicAdd(&p.counters->next_query, 1u);
+        qi = __shfl_sync(kFull, qi, 0);
+        if (qi >= p.nq) break;
+
+        const float* q = p.queries + static_cast<size_t>(qi) * p.dim;
+        for (uint32_t d = lane; d < p.row_stride; d += 32) qsm[d] = d < p.dim ? __ldg(q + d) : 0.0f;
+        for (uint32_t i = lane; i < p.filter_words; i += 32) filt[i] = (FM == kHash) ? kNoNode : 0u;
+        if (lane == 0) cids[0] = p.entry;
+        __syncwarp();
+        const bool team_ok = DM != kSeq && query_integer_exact(qsm, p.dim, p.team_qlo, p.team_qhi);
+        if (DM != kSeq && !team_ok && lane == 0) atomicAdd(&p.counters->team_fallbacks, 1u);
+        if (DM == kU8 && team_ok) pack_query_u8(qsm, p.dim, p.row_bytes, q8, lane);
+
+        score_direct<DM>(p, 1, cids, cdist, qsm, q8, lane, team_ok);
+        uint64_t beam[RX];
+#pragma unroll
+        for (int r = 0; r < RX; ++r) beam[r] = kEmptyKey;
+        if (lane == 0) {
+            beam[0] = make_key(cdist[0], p.entry);
+            if (FM == kHash) hash_insert(filt, fmask, fshift, p.entry, err);
+            else bloom_set(filt, fmask, p.entry);
+        }
+        uint32_t filled = 1;
+        uint32_t E = 0, D = 1;
+        __syncwarp();
+
+        for (int iter = 0; iter < p.max_iterations; ++iter) {
+            uint32_t cur;
+            if (!beam_pick<RX>(beam, lane, cur)) break;
+            ++E;
+            __syncwarp();   // earlier reads of the block and of cids/cdist are done
+
+            if (lane == 0) bulk_load(blk, p.nb + static_cast<size_t>(cur) * p.nb_stride, p.nb_stride, mbar);
+            if (!mbar_wait(mbar, phase)) {
+                // give the copy in flight a last bounded chance, then leave:
+                // the host reads the flag and reports BS_ERR_KERNEL
+                mbar_wait(mbar, phase);
+                if (lane == 0) atomicOr(&p.counters->error_flags, err | kErrWaitTimeout);
+                return;
+            }
+            phase ^= 1u;
+
+            uint32_t c[RY];
+            bool fresh[RY];
+#pragma unroll
+            for (int r = 0; r < RY; ++r) {
+                const uint32_t pos = static_cast<uint32_t>(r) * 32u + lane;
+                c[r] = pos < deg ? blk_adj[pos] : kNoNode;
+            }
+
+            if (FM == kHash) {
+                if (filled + deg > p.filter_limit) {
+                    // exact for L2: a node that left the beam can never re-enter
+                    for (uint32_t i = lane; i < p.filter_words; i += 32) filt[i] = kNoNode;
+                    __syncwarp();
+                    uint32_t cnt = 0;
+#pragma unroll
+                    for (int r = 0; r < RX; ++r) {
+                        const bool v = beam[r] != kEmptyKey;
+                        if (v) hash_insert(filt, fmask, fshift, key_id(beam[r]), err);
+                        cnt += __popc(__ballot_sync(kFull, v));
+                    }
+                    filled = cnt;
+                    __syncwarp();
+                }
+#pragma unroll
+                for (int r = 0; r < RY; ++r)
+                    fresh[r] = c[r] < p.n && hash_insert(filt, fmask, fshift, c[r], err) != 0;
+            } else {
+                bool valid[RY], present[RY];
+#pragma unroll
+                for (int r = 0; r < RY; ++r) {
+                    const uint32_t pos = static_cast<uint32_t>(r) * 32u + lane;
+                    bool v = c[r] < p.n;
+                    for (uint32_t j = 0; j < pos && v; ++j) v = blk_adj[j] != c[r];
+                    valid[r] = v;
+                    present[r] = v ? bloom_test(filt, fmask, c[r]) : true;
+                }
+                __syncwarp();
+#pragma unroll
+                for (int r = 0; r < RY; ++r) {
+                    if (valid[r]) bloom_set(filt, fmask, c[r]);
+                    fresh[r] = valid[r] && !present[r];
+                }
+                __syncwarp();
+            }
+
+            uint32_t m = 0;
+#pragma unroll
+            for (int r = 0; r < RY; ++r) {
+                const unsigned b = __ballot_sync(kFull, fresh[r]);
+                if (fresh[r]) {
+                    const uint32_t at = m + __popc(b & lt_mask);
+                    cids[at] = c[r];
+                    cpos[at] = static_cast<uint32_t>(r) * 32u + lane;
+                }
+                m += __popc(b);
+            }
+            __syncwarp();
+
+            if (m) {
+                filled += m;
+                D += m;
+                score_block<DM>(p, m, cpos, blk_rows, cdist, qsm, q8, lane, team_ok);
+                const uint64_t bound = beam_bound<RX>(beam, p.topk);
+                unsigned cnt = 0;
+#pragma unroll
+                for (int r = 0; r < RY; ++r) {
+                    const uint32_t s = static_cast<uint32_t>(r) * 32u + lane;
+                    const uint64_t k = s < m ? make_key(cdist[s], cids[s]) : kEmptyKey;
+                    const bool keep = k < bound;
+                    const unsigned b = __ballot_sync(kFull, keep);
+                    if (keep) ckeys[cnt + __popc(b & lt_mask)] = k;
+                    cnt += __popc(b);
+                }
+                if (cnt) {
+                    __syncwarp();
+                    beam_merge_compact<RX, RY>(beam, ckeys, cnt, lane, p.topk);
+                }
+            }
+
+            if (FM == kBloom && p.reset_interval > 0 && (iter + 1) % p.reset_interval == 0) {
+                __syncwarp();
+                for (uint32_t i = lane; i < p.filter_words; i += 32) filt[i] = 0u;
+                __syncwarp();
+#pragma unroll
+                for (int r = 0; r < RX; ++r)
+                    if (beam[r] != kEmptyKey) bloom_set(filt, fmask, key_id(beam[r]));
+                __syncwarp();
+            }
+        }
+
+        uint32_t* oid = p.out_ids + static_cast<size_t>(qi) * p.K;
+        float* odist = p.out_dists ? p.out_dists + static_cast<size_t>(qi) * p.K : nullptr;
+#pragma unroll
+        for (int r = 0; r < RX; ++r) {
+            const uint32_t pos = static_cast<uint32_t>(r) * 32u + lane;
+            if (pos < p.K) {
+                const bool v = beam[r] != kEmptyKey;
+                oid[pos] = v ? key_id(beam[r]) : kNoNode;
+                if (odist) odist[pos] = v ? key_dist(beam[r]) : FLT_MAX;
+            }
+        }
+        for (uint32_t pos = 32u * RX + lane; pos < p.K; pos += 32) {
+            oid[pos] = kNoNode;
+            if (odist) odist[pos] = FLT_MAX;
+        }
+        if (lane == 0) {
+            atomicAdd(&p.counters->expansions, static_cast<unsigned long long>(E));
+            atomicAdd(&p.counters->distances, static_cast<unsigned long long>(D));
+            if (p.q_stats) {
+                p.q_stats[2 * static_cast<size_t>(qi)] = E;
+                p.q_stats[2 * static_cast<size_t>(qi) + 1] = D;
+            }
+        }
+        __syncwarp();
+    }
+    if (lane == 0 && err) atomicOr(&p.counters->error_flags, err);
+}
+
+// One warp per node: the node's adjacency row, then each neighbour's row
+// (zeros for an id outside the graph), 16 bytes per lane per step.
+__global__ void k_build_nb(const SearchParams p, unsigned char* __restrict__ out) {
+    const unsigned lane = threadIdx.x & 31u;
+    const uint64_t warp = (static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const uint64_t nwarps = (static_cast<uint64_t>(gridDim.x) * blockDim.x) >> 5;
+    const uint32_t src_bytes = p.vecs8 ? p.row_bytes : p.row_stride * 4u;
+    const uint32_t chunks = p.nb_pitch / 16u;
+    for (uint64_t v = warp; v < p.n; v += nwarps) {
+        unsigned char* dst = out + v * p.nb_stride;
+        const uint32_t* arow = p.adj + v * p.degree;
+        for (uint32_t i = lane; i < p.nb_adj_bytes / 4u; i += 32)
+            reinterpret_cast<uint32_t*>(dst)[i] = i < p.degree ? arow[i] : kNoNode;
+        const uint32_t total = p.degree * chunks;
+        for (uint32_t t = lane; t < total; t += 32) {
+            const uint32_t i = t / chunks, ch = t - i * chunks;
+            const uint32_t child = arow[i];
+            uint4 val = make_uint4(0u, 0u, 0u, 0u);
+            if (child < p.n && ch * 16u < src_bytes) {
+                const unsigned char* src = p.vecs8 ? p.vecs8 + static_cast<size_t>(child) * p.row_bytes
+                                                   : reinterpret_cast<const unsigned char*>(
+                                                         p.vecs + static_cast<size_t>(child) * p.row_stride);
+                val = *reinterpret_cast<const uint4*>(src + ch * 16u);
+            }
+            *reinterpret_cast<uint4*>(dst + p.nb_adj_bytes + static_cast<size_t>(i) * p.nb_pitch + ch * 16u) = val;
+        }
+    }
+}
+
+using KernelFn = void (*)(SearchParams);
+
+template <int RX, int RY>
+KernelFn pick_nb(int dm, int fm) {
+    if (dm == kSeq) return fm == kHash ? k_search_nb<RX, RY, kSeq, kHash> : k_search_nb<RX, RY, kSeq, kBloom>;
+    if (dm == kU8) return fm == kHash ? k_search_nb<RX, RY, kU8, kHash> : k_search_nb<RX, RY, kU8, kBloom>;
+    return fm == kHash ? k_search_nb<RX, RY, kTeam, kHash> : k_search_nb<RX, RY, kTeam, kBloom>;
+}
+
+KernelFn select_nb(int regx, int regy, int dm, int fm) {
+    if (regy == 1) {
+        switch (regx) {
+            case 1: return pick_nb<1, 1>(dm, fm);
+            case 2: return pick_nb<2, 1>(dm, fm);
+            case 4: return pick_nb<4, 1>(dm, fm);
+            case 8: return pick_nb<8, 1>(dm, fm);
+            case 16: return pick_nb<16, 1>(dm, fm);
+        }
+    } else if (regy == 2) {
+        switch (regx) {
+            case 2: return pick_nb<2, 2>(dm, fm);
+            case 4: return pick_nb<4, 2>(dm, fm);
+            case 8: return pick_nb<8, 2>(dm, fm);
+            case 16: return pick_nb<16, 2>(dm, fm);
+        }
+    }
+    return nullptr;
+}
+
+}  // namespace
+
+cudaError_t launch_search_nb(const SearchParams& p, const LaunchShape& shape, int num_sms, cudaStream_t stream) {
+    KernelFn fn = select_nb(shape.regx, shape.regy, shape.dmode, shape.fmode);
+    if (!fn) return cudaErrorInvalidValue;
+    const int threads = 32 * shape.warps_per_block;
+    const size_t smem = static_cast<size_t>(shape.smem_per_warp) * shape.warps_per_block;
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    int per_sm = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, smem);
+    if (e != cudaSuccess) return e;
+    if (per_sm < 1) return cudaErrorInvalidConfiguration;
+    const uint64_t want = (static_cast<uint64_t>(p.nq) + shape.warps_per_block - 1) / shape.warps_per_block;
+    const uint64_t cap = static_cast<uint64_t>(per_sm) * static_cast<uint64_t>(num_sms);
+    const unsigned grid = static_cast<unsigned>(want < cap ? want : cap);
+    if (grid == 0) return cudaSuccess;
+    fn<<<grid, threads, smem, stream>>>(p);
+    return cudaGetLastError();
+}
+
+cudaError_t build_neighbourhood_blocks(const SearchParams& p, unsigned char* out, cudaStream_t stream) {
+    const uint64_t warps = p.n;
+    const uint64_t blocks64 = (warps + 7) / 8;
+    const unsigned blocks = static_cast<unsigned>(blocks64 < 65535ull * 8 ? blocks64 : 65535ull * 8);
+    k_build_nb<<<blocks, 256, 0, stream>>>(p, out);
+    return cudaGetLastError();
+}
+
+}  // namespace bsb

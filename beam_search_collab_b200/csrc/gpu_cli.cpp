@@ -21,7 +21,7 @@
 #include <unordered_set>
 #include <vector>
 
-#include "../../include/bsearch.h"
+#include "bsearch.h"
 #include "bs_io.hpp"
 #include "json_lite.hpp"
 

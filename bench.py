@@ -85,6 +85,12 @@ class ClockSampler:
                  "-lms", "20"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            # nvidia-smi needs a moment to start: sample from before the timed
+            # region begins, not after it ended
+            t0 = time.time()
+            while not self.lines and time.time() - t0 < 5.0:
+                time.sleep(0.01)
+            self.lines.clear()
         except Exception:
             self.proc = None
         return self
@@ -204,10 +210,14 @@ def run_ours(args, rank, world, local_rank):
     _, _, st = ix.search(q_dev, params)
     torch.cuda.synchronize()
     dim, deg = base.shape[1], edges.shape[1]
-    # query read + adjacency rows + candidate rows as stored (u8 copy: 1 B/dim)
-    # + ids and distances written
-    alg_bytes = (NQ_PER_GPU * 4 * dim + st.expansions * 4 * deg + st.distances * st.row_bytes
-                 + NQ_PER_GPU * 8 * K)
+    # query read + per expansion either one neighbourhood block (adjacency row
+    # and all neighbour rows, copied whole) or the adjacency row and the rows of
+    # the scored candidates as stored (u8 copy: 1 B/dim) + ids and distances
+    if st.block_bytes:
+        per_expansion = st.expansions * st.block_bytes
+    else:
+        per_expansion = st.expansions * 4 * deg + st.distances * st.row_bytes
+    alg_bytes = NQ_PER_GPU * 4 * dim + per_expansion + NQ_PER_GPU * 8 * K
 
     stream = torch.cuda.Stream(device=dev)
     flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
@@ -298,6 +308,8 @@ def run_ours(args, rank, world, local_rank):
             "entry_point": entry,
             "distance_path": ("integer-exact" if st.integer_exact else "sequential per lane")
                              + f", stored row {st.row_bytes} B",
+            "layout": (f"neighbourhood blocks, {st.block_bytes} B bulk copy per expansion"
+                       if st.block_bytes else "gather"),
             "expansions_per_query": round(st.expansions / NQ_PER_GPU, 2),
             "distances_per_query": round(st.distances / NQ_PER_GPU, 2),
             "l2": "256 MiB write before every timed step (outside the timed window); index 640 MB > L2",
@@ -421,7 +433,7 @@ def profile_run(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--mode", default="warp4")

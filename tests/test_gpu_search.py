@@ -60,12 +60,22 @@ def test_small_filter_forces_resets_and_stays_exact(indexes, name):
 
 
 @pytest.mark.parametrize("name", G.NAMES)
-def test_distance_counter_matches_oracle_when_filter_never_resets(indexes, name):
-    g, ix = indexes[name]
-    ref = O.search(g.base, g.edges, g.queries, K=10, topk_size=64, entry=g.entry)
-    _, _, st = ix.search(g.queries, mode="warp1", K=10, topk_size=64, filter_capacity=1 << 14)
-    assert st.expansions == ref.stats.expansions
-    assert st.distances == ref.stats.distances
+def test_distance_counter_matches_oracle_when_filter_never_resets(indexes, name, monkeypatch):
+    """Gather layout with a visited table large enough never to reset: every
+    pushed node is scored exactly once, as in the reference CPU search.  (The
+    block layout sizes its table to the beam and may score a forgotten node
+    again; its counter is then larger, its results the same.)"""
+    g, _ = indexes[name]
+    monkeypatch.setenv("BSEARCH_LAYOUT", "gather")
+    ix = B.Index.from_arrays(g.base, g.edges)
+    monkeypatch.delenv("BSEARCH_LAYOUT")
+    try:
+        ref = O.search(g.base, g.edges, g.queries, K=10, topk_size=64, entry=g.entry)
+        _, _, st = ix.search(g.queries, mode="warp1", K=10, topk_size=64, filter_capacity=1 << 14)
+        assert st.expansions == ref.stats.expansions
+        assert st.distances == ref.stats.distances
+    finally:
+        ix.close()
 
 
 @pytest.mark.parametrize("name", ["f48", "s96d64"])
@@ -118,6 +128,27 @@ def test_integer_path_and_sequential_path_agree(indexes, monkeypatch):
     assert st_s.integer_exact == 0
     assert np.array_equal(ids_t, ids_s)
     assert np.array_equal(d_t.view(np.uint32), d_s.view(np.uint32))
+
+
+@pytest.mark.parametrize("name", G.NAMES)
+def test_gather_layout_and_block_layout_agree(indexes, name, monkeypatch):
+    """The default index keeps neighbourhood blocks (one bulk copy per
+    expansion); BSEARCH_LAYOUT=gather builds the plain layout.  Both run the
+    same search and must agree bit for bit, in exact and Bloom modes."""
+    g, ix_blocks = indexes[name]
+    monkeypatch.setenv("BSEARCH_LAYOUT", "gather")
+    ix_gather = B.Index.from_arrays(g.base, g.edges)
+    monkeypatch.delenv("BSEARCH_LAYOUT")
+    try:
+        for mode, K, topk in (("warp4", 10, 64), ("base", 50, 160), ("bwarp2", 10, 64)):
+            a = ix_blocks.search(g.queries, mode=mode, K=K, topk_size=topk)
+            b = ix_gather.search(g.queries, mode=mode, K=K, topk_size=topk)
+            assert np.array_equal(a[0], b[0])
+            assert np.array_equal(a[1].view(np.uint32), b[1].view(np.uint32))
+            assert a[2].expansions == b[2].expansions
+            assert a[2].distances >= b[2].distances   # the block layout may re-score forgotten nodes
+    finally:
+        ix_gather.close()
 
 
 def test_byte_storage_and_float_storage_agree(indexes, monkeypatch):
