@@ -212,10 +212,12 @@ void pack_u8_rows(const float* v, uint64_t n, int32_t dim, uint32_t row_bytes, u
 // per node, so that an expansion is one bulk copy).  Built when the blocks
 // take at most 40% of the device's free memory; BSEARCH_LAYOUT=gather turns
 // them off.  Row pitch: the stored row, grown to an odd number of 16-byte
-// units for f32 rows so that lanes reading one row each hit distinct banks.
+// units for f32 rows so that lanes reading one row each hit distinct banks
+// (u8 rows rotate their chunks instead).
 cudaError_t build_blocks(bs_index* ix) {
     const char* env = std::getenv("BSEARCH_LAYOUT");
     if (env && std::strcmp(env, "gather") == 0) return cudaSuccess;
+    if (ix->degree > 64) return cudaSuccess;                    // the search supports degree <= 64
     uint32_t pitch;
     if (ix->u8) {
         pitch = ix->row_bytes;

@@ -60,15 +60,15 @@ struct SearchParams {
     uint32_t row_bytes;         // dim rounded up to 16
     const uint32_t* adj;        // [n][degree] u32
     // neighbourhood blocks (null: gather layout): per node, its adjacency row
-    // (nb_adj_bytes) then the rows of its degree neighbours, nb_pitch bytes
-    // apart; nb_stride bytes per node, all multiples of 16
+    // (nb_adj_bytes; repeated ids replaced by 0xffffffff) then the rows of its
+    // degree neighbours, nb_pitch bytes apart (u8 rows: 16-byte chunks
+    // rotated per row); nb_stride bytes per node, all multiples of 16
     const unsigned char* nb;
     uint32_t nb_stride;
     uint32_t nb_adj_bytes;
     uint32_t nb_pitch;
     uint32_t off_block;         // per-warp copy of one block
     uint32_t off_mbar;          // per-warp mbarrier (8 bytes)
-    uint32_t off_cpos;          // block positions of the compacted candidates
     uint64_t n;
     uint32_t dim;
     uint32_t row_stride;        // floats per stored row (dim rounded up to 4)

@@ -285,9 +285,9 @@ cudaError_t plan_search(SearchParams& p, LaunchShape& shape, size_t max_smem_opt
     } else if (shape.fmode == kHash) {
         // Room for the beam plus several rows between resets, at <= 3/4 load.
         const uint64_t need = (static_cast<uint64_t>(p.topk) + 4ull * p.degree) * 4ull / 3ull + 1;
-        // With neighbourhood blocks a forgotten node costs only a distance
-        // over rows already in shared memory, so the table is sized to the
-        // beam (more resets, more resident warps) instead of filter_capacity.
+        // With neighbourhood blocks the table only holds ids that passed
+        // into the beam, so it is sized to the beam instead of
+        // filter_capacity (more resident warps).
         const uint64_t want = p.nb != nullptr ? need : (p.filter_slots > need ? p.filter_slots : need);
         const uint32_t slots = pow2_at_least(want);
         p.filter_slots = slots < 64 ? 64 : slots;
@@ -326,10 +326,8 @@ cudaError_t plan_search(SearchParams& p, LaunchShape& shape, size_t max_smem_opt
     }
     p.off_stage = off;
     if (p.nb != nullptr && p.codes == nullptr) {
-        // neighbourhood blocks: candidate positions, the mbarrier and one
-        // block copy replace the staging area
-        p.off_cpos = off;
-        off = align16(off + cand * 4u);
+        // neighbourhood blocks: the mbarrier and one block copy replace the
+        // staging area
         p.off_mbar = off;
         off = align16(off + 8u);
         p.off_block = off;

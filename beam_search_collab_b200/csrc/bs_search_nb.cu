@@ -1,19 +1,35 @@
 // bs_search_nb.cu -- the exact L2 beam search (modes base, warp1..8,
 // bwarp1..8) over neighbourhood blocks.
 //
-// Same semantics as bs_search.cu (the reference CPU search,
-// include/cpu_search_base.hpp:22-82); only the memory path differs.  The
-// gather layout needs two dependent round trips per expansion -- the node's
-// adjacency row, then the rows of its unvisited neighbours.  Here every node
-// owns one contiguous block in HBM:
+// Same results as bs_search.cu (the reference CPU search,
+// include/cpu_search_base.hpp:22-82); the memory path and the order of the
+// work differ.  The gather layout needs two dependent round trips per
+// expansion -- the node's adjacency row, then the rows of its unvisited
+// neighbours.  Here every node owns one contiguous block in HBM:
 //
 //     [ adjacency row (degree u32, padded to 16 B) | row of neighbour 0 | ... ]
 //
 // so an expansion is ONE bulk copy (cp.async.bulk global->shared, completion
-// counted on a per-warp mbarrier) of the expanded node's block, after which
-// the visited filter, the distances and the merge all read shared memory.
-// The blocks trade capacity for latency (C2: 4.2 KB per node, 4.2 GB for
-// 1M nodes); the host builds them only when they fit the device comfortably.
+// counted on a per-warp mbarrier) of the expanded node's block.  With every
+// neighbour row already in shared memory, lane i scores row i outright, and
+// the exact visited set is consulted only by the candidates whose key beats
+// the beam's T-th key:
+//
+//   * a node seen before that is not in the beam has a key at or above the
+//     current T-th key -- it left the beam, or never entered it, while T
+//     better keys were present, and the T-th key never rises -- so the
+//     bound drops it, as the reference's visited set would;
+//   * a candidate below the bound that was seen before is therefore in the
+//     beam, and the table (every id that ever passed into the beam; rebuilt
+//     from the beam when full) finds it.
+//
+// The Bloom modes keep the reference's filter in front of the merge (its
+// false positives skip nodes).  Repeated ids inside one adjacency row are
+// replaced by "no node" when the blocks are built: the reference skips a
+// repeat because the first occurrence marked it visited.
+//
+// The blocks trade capacity for latency (C2: 4.2 KB per node, 4.2 GB for 1M
+// nodes); the host builds them only when they fit the device comfortably.
 #include <cfloat>
 #include <cstdio>
 
@@ -74,101 +90,99 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* mbar, unsigned phase) {
 
 // ------------------------------------------------------------- scoring
 
-// Distances of the compacted candidates s < m whose rows sit in the block at
-// positions cpos[s].  Same arithmetic as the gather scorers in bs_score.cuh.
-// Rows come from shared memory, so a few per team in flight suffice (and keep
-// the register count, hence the resident warps, up).
-constexpr int kSlots = 4;
+// Position of 16-byte chunk c of neighbour row s inside a block of u8 rows
+// (nch chunks per row): the chunks of each group of 8 are rotated by s, so
+// the 8 lanes of one shared-memory phase, reading chunk c of 8 consecutive
+// rows, touch 8 different bank groups.
+__device__ __forceinline__ uint32_t nb_chunk_pos(uint32_t c, uint32_t s, uint32_t nch) {
+    const uint32_t g0 = c & ~7u;
+    const uint32_t g = nch - g0 < 8u ? nch - g0 : 8u;
+    return g0 + (c - g0 + s) % g;
+}
 
+__device__ __forceinline__ void dp4a_chunk(const uint4 v, const uint4 q, unsigned& xx, unsigned& qx) {
+    xx = __dp4a(v.x, v.x, xx); qx = __dp4a(q.x, v.x, qx);
+    xx = __dp4a(v.y, v.y, xx); qx = __dp4a(q.y, v.y, qx);
+    xx = __dp4a(v.z, v.z, xx); qx = __dp4a(q.z, v.z, qx);
+    xx = __dp4a(v.w, v.w, xx); qx = __dp4a(q.w, v.w, qx);
+}
+
+__device__ __forceinline__ float seq_step(float acc, float q, float x) {
+    const float t = __fsub_rn(q, x);
+    return __fadd_rn(acc, __fmul_rn(t, t));
+}
+
+// Distance from the query to neighbour row s of the block, computed by the
+// calling lane alone.
+//   kU8, integer query : sum (q-x)^2 = sum x^2 - 2 sum q.x + sum q^2 over the
+//                        bytes with __dp4a -- exact integers, hence the
+//                        reference's fp32 value (the host only selects this
+//                        path when dim * 255^2 fits 24 bits)
+//   kTeam, integer data: fused multiply-add; every partial sum is an exact
+//                        integer, so any order gives the reference's bits
+//   otherwise          : the reference's sequential fold, d = 0..dim-1, each
+//                        operation rounded separately
+//                        (include/cpu_search_base.hpp:29-37); the zero pad
+//                        lanes add +0 and change nothing
 template <int DM>
-__device__ __forceinline__ void score_block(const SearchParams& p, uint32_t m, const uint32_t* cpos,
-                                            const unsigned char* rows, float* cdist, const float* qsm,
-                                            const uint32_t* q8, unsigned lane, bool team_ok) {
-    if (DM == kU8 && team_ok) {
-        const unsigned team = lane >> 3, tl = lane & 7u;
-        const unsigned char* qb = reinterpret_cast<const unsigned char*>(q8);
-        const unsigned qq = q8[p.row_bytes / 4u];
-        for (uint32_t s0 = 0; s0 < m; s0 += 4u * kSlots) {
-            unsigned xx[kSlots], qx[kSlots];
-#pragma unroll
-            for (int j = 0; j < kSlots; ++j) { xx[j] = 0u; qx[j] = 0u; }
-            for (uint32_t off = tl * 16u; off < p.row_bytes; off += 128u) {
-                const uint4 q = *reinterpret_cast<const uint4*>(qb + off);
-#pragma unroll
-                for (int j = 0; j < kSlots; ++j) {
-                    const uint32_t s = s0 + team + 4u * j;
-                    if (s < m) {
-                        const uint4 v = *reinterpret_cast<const uint4*>(rows + cpos[s] * p.nb_pitch + off);
-                        xx[j] = __dp4a(v.x, v.x, xx[j]); qx[j] = __dp4a(q.x, v.x, qx[j]);
-                        xx[j] = __dp4a(v.y, v.y, xx[j]); qx[j] = __dp4a(q.y, v.y, qx[j]);
-                        xx[j] = __dp4a(v.z, v.z, xx[j]); qx[j] = __dp4a(q.z, v.z, qx[j]);
-                        xx[j] = __dp4a(v.w, v.w, xx[j]); qx[j] = __dp4a(q.w, v.w, qx[j]);
+__device__ __forceinline__ float block_row_dist(const SearchParams& p, const unsigned char* rows, uint32_t s,
+                                                const float* qsm, const unsigned char* qb, uint32_t qq,
+                                                bool team_ok) {
+    const unsigned char* row = rows + static_cast<size_t>(s) * p.nb_pitch;
+    if (DM == kU8) {
+        const uint32_t nch = p.row_bytes / 16u;
+        if (team_ok) {
+            unsigned xx = 0u, qx = 0u;
+            if ((nch & 7u) == 0u) {
+                for (uint32_t g0 = 0; g0 < nch; g0 += 8u) {
+#pragma unroll 4
+                    for (uint32_t t = 0; t < 8u; ++t) {
+                        const uint4 v = *reinterpret_cast<const uint4*>(row + (g0 + ((s + t) & 7u)) * 16u);
+                        const uint4 q = *reinterpret_cast<const uint4*>(qb + (g0 + t) * 16u);
+                        dp4a_chunk(v, q, xx, qx);
                     }
                 }
-            }
-#pragma unroll
-            for (int j = 0; j < kSlots; ++j) {
-                unsigned a = xx[j] - 2u * qx[j];
-                a += __shfl_xor_sync(kFull, a, 4);
-                a += __shfl_xor_sync(kFull, a, 2);
-                a += __shfl_xor_sync(kFull, a, 1);
-                const uint32_t s = s0 + team + 4u * j;
-                if (tl == 0 && s < m) cdist[s] = static_cast<float>(a + qq);
-            }
-        }
-    } else if (DM == kTeam && team_ok) {
-        const unsigned team = lane >> 3, tl = lane & 7u;
-        for (uint32_t s0 = 0; s0 < m; s0 += 4u * kSlots) {
-            float acc[kSlots];
-#pragma unroll
-            for (int j = 0; j < kSlots; ++j) acc[j] = 0.0f;
-            for (uint32_t d = tl * 4u; d < p.row_stride; d += 32u) {
-                const float4 qv = *reinterpret_cast<const float4*>(qsm + d);
-#pragma unroll
-                for (int j = 0; j < kSlots; ++j) {
-                    const uint32_t s = s0 + team + 4u * j;
-                    if (s < m) {
-                        const float4 v = *reinterpret_cast<const float4*>(rows + cpos[s] * p.nb_pitch + 4u * d);
-                        float t;
-                        t = qv.x - v.x; acc[j] = fmaf(t, t, acc[j]);
-                        t = qv.y - v.y; acc[j] = fmaf(t, t, acc[j]);
-                        t = qv.z - v.z; acc[j] = fmaf(t, t, acc[j]);
-                        t = qv.w - v.w; acc[j] = fmaf(t, t, acc[j]);
-                    }
+            } else {
+                for (uint32_t c = 0; c < nch; ++c) {
+                    const uint4 v = *reinterpret_cast<const uint4*>(row + nb_chunk_pos(c, s, nch) * 16u);
+                    const uint4 q = *reinterpret_cast<const uint4*>(qb + c * 16u);
+                    dp4a_chunk(v, q, xx, qx);
                 }
             }
-#pragma unroll
-            for (int j = 0; j < kSlots; ++j) {
-                float a = acc[j];
-                a += __shfl_xor_sync(kFull, a, 4);
-                a += __shfl_xor_sync(kFull, a, 2);
-                a += __shfl_xor_sync(kFull, a, 1);
-                const uint32_t s = s0 + team + 4u * j;
-                if (tl == 0 && s < m) cdist[s] = a;
-            }
+            return static_cast<float>(xx - 2u * qx + qq);
         }
-    } else {
-        // the reference's sequential fold, one lane per row
-        for (uint32_t c0 = 0; c0 < m; c0 += 32) {
-            const uint32_t s = c0 + lane;
-            if (s < m) {
-                const unsigned char* r = rows + cpos[s] * p.nb_pitch;
-                float v;
-                if (DM == kU8) {
-                    float acc = 0.0f;
-                    for (uint32_t d = 0; d < p.dim; ++d) {
-                        const float t = __fsub_rn(qsm[d], static_cast<float>(r[d]));
-                        acc = __fadd_rn(acc, __fmul_rn(t, t));
-                    }
-                    v = acc;
-                } else {
-                    v = l2_seq(qsm, reinterpret_cast<const float*>(r), p.dim);
-                }
-                cdist[s] = v;
-            }
+        float acc = 0.0f;
+        for (uint32_t c = 0; c < nch; ++c) {
+            const unsigned char* chunk = row + nb_chunk_pos(c, s, nch) * 16u;
+            const uint32_t d0 = c * 16u;
+            const uint32_t n = p.dim - d0 < 16u ? p.dim - d0 : 16u;
+            for (uint32_t k = 0; k < n; ++k) acc = seq_step(acc, qsm[d0 + k], static_cast<float>(chunk[k]));
         }
+        return acc;
     }
-    __syncwarp();
+    const float4* r4 = reinterpret_cast<const float4*>(row);
+    const float4* q4 = reinterpret_cast<const float4*>(qsm);
+    const uint32_t units = p.row_stride / 4u;
+    float acc = 0.0f;
+    if (DM == kTeam && team_ok) {
+        for (uint32_t u = 0; u < units; ++u) {
+            const float4 v = r4[u], q = q4[u];
+            float t;
+            t = q.x - v.x; acc = fmaf(t, t, acc);
+            t = q.y - v.y; acc = fmaf(t, t, acc);
+            t = q.z - v.z; acc = fmaf(t, t, acc);
+            t = q.w - v.w; acc = fmaf(t, t, acc);
+        }
+        return acc;
+    }
+    for (uint32_t u = 0; u < units; ++u) {
+        const float4 v = r4[u], q = q4[u];
+        acc = seq_step(acc, q.x, v.x);
+        acc = seq_step(acc, q.y, v.y);
+        acc = seq_step(acc, q.z, v.z);
+        acc = seq_step(acc, q.w, v.w);
+    }
+    return acc;
 }
 
 // Exact distance of one node straight from the gather layout (the entry).
@@ -193,11 +207,11 @@ __global__ void __launch_bounds__(256) k_search_nb(const SearchParams p) {
     unsigned char* ws = smem_raw + static_cast<size_t>(threadIdx.x >> 5) * p.smem_per_warp;
     float* qsm = reinterpret_cast<float*>(ws);
     uint32_t* q8 = reinterpret_cast<uint32_t*>(ws + p.off_q8);
+    const unsigned char* qb = ws + p.off_q8;
     uint32_t* filt = reinterpret_cast<uint32_t*>(ws + p.off_filter);
     uint32_t* cids = reinterpret_cast<uint32_t*>(ws + p.off_cids);
     float* cdist = reinterpret_cast<float*>(ws + p.off_cdist);
     uint64_t* ckeys = reinterpret_cast<uint64_t*>(ws + p.off_keys);
-    uint32_t* cpos = reinterpret_cast<uint32_t*>(ws + p.off_cpos);
     uint64_t* mbar = reinterpret_cast<uint64_t*>(ws + p.off_mbar);
     unsigned char* blk = ws + p.off_block;
     const uint32_t* blk_adj = reinterpret_cast<const uint32_t*>(blk);
@@ -226,6 +240,7 @@ __global__ void __launch_bounds__(256) k_search_nb(const SearchParams p) {
         const bool team_ok = DM != kSeq && query_integer_exact(qsm, p.dim, p.team_qlo, p.team_qhi);
         if (DM != kSeq && !team_ok && lane == 0) atomicAdd(&p.counters->team_fallbacks, 1u);
         if (DM == kU8 && team_ok) pack_query_u8(qsm, p.dim, p.row_bytes, q8, lane);
+        const uint32_t qq = (DM == kU8 && team_ok) ? q8[p.row_bytes / 4u] : 0u;
 
         score_direct<DM>(p, 1, cids, cdist, qsm, q8, lane, team_ok);
         uint64_t beam[RX];
@@ -244,7 +259,7 @@ __global__ void __launch_bounds__(256) k_search_nb(const SearchParams p) {
             uint32_t cur;
             if (!beam_pick<RX>(beam, lane, cur)) break;
             ++E;
-            __syncwarp();   // earlier reads of the block and of cids/cdist are done
+            __syncwarp();   // earlier reads of the block and of ckeys are done
 
             if (lane == 0) bulk_load(blk, p.nb + static_cast<size_t>(cur) * p.nb_stride, p.nb_stride, mbar);
             if (!mbar_wait(mbar, phase)) {
@@ -257,16 +272,47 @@ __global__ void __launch_bounds__(256) k_search_nb(const SearchParams p) {
             phase ^= 1u;
 
             uint32_t c[RY];
-            bool fresh[RY];
+            bool live[RY];
 #pragma unroll
             for (int r = 0; r < RY; ++r) {
                 const uint32_t pos = static_cast<uint32_t>(r) * 32u + lane;
                 c[r] = pos < deg ? blk_adj[pos] : kNoNode;
+                live[r] = c[r] < p.n;
+            }
+            if (FM == kBloom) {
+                // reference order: every child tested against the filter as it
+                // was before this expansion, then every child set
+                bool present[RY];
+#pragma unroll
+                for (int r = 0; r < RY; ++r) present[r] = live[r] && bloom_test(filt, fmask, c[r]);
+                __syncwarp();
+#pragma unroll
+                for (int r = 0; r < RY; ++r) {
+                    if (live[r]) bloom_set(filt, fmask, c[r]);
+                    live[r] = live[r] && !present[r];
+                }
             }
 
-            if (FM == kHash) {
-                if (filled + deg > p.filter_limit) {
-                    // exact for L2: a node that left the beam can never re-enter
+            // one row per lane, straight from the block
+            uint64_t k[RY];
+            bool keep[RY];
+            const uint64_t bound = beam_bound<RX>(beam, p.topk);
+            uint32_t nkeep = 0;
+#pragma unroll
+            for (int r = 0; r < RY; ++r) {
+                float d = 0.0f;
+                if (live[r])
+                    d = block_row_dist<DM>(p, blk_rows, static_cast<uint32_t>(r) * 32u + lane, qsm, qb, qq, team_ok);
+                k[r] = live[r] ? make_key(d, c[r]) : kEmptyKey;
+                D += __popc(__ballot_sync(kFull, live[r]));
+                keep[r] = k[r] < bound;
+                nkeep += __popc(__ballot_sync(kFull, keep[r]));
+            }
+
+            if (FM == kHash && nkeep) {
+                if (filled + nkeep > p.filter_limit) {
+                    // keep only the beam's ids: every other id seen so far is
+                    // at or above the bound for good
                     for (uint32_t i = lane; i < p.filter_words; i += 32) filt[i] = kNoNode;
                     __syncwarp();
                     uint32_t cnt = 0;
@@ -281,58 +327,20 @@ __global__ void __launch_bounds__(256) k_search_nb(const SearchParams p) {
                 }
 #pragma unroll
                 for (int r = 0; r < RY; ++r)
-                    fresh[r] = c[r] < p.n && hash_insert(filt, fmask, fshift, c[r], err) != 0;
-            } else {
-                bool valid[RY], present[RY];
-#pragma unroll
-                for (int r = 0; r < RY; ++r) {
-                    const uint32_t pos = static_cast<uint32_t>(r) * 32u + lane;
-                    bool v = c[r] < p.n;
-                    for (uint32_t j = 0; j < pos && v; ++j) v = blk_adj[j] != c[r];
-                    valid[r] = v;
-                    present[r] = v ? bloom_test(filt, fmask, c[r]) : true;
-                }
-                __syncwarp();
-#pragma unroll
-                for (int r = 0; r < RY; ++r) {
-                    if (valid[r]) bloom_set(filt, fmask, c[r]);
-                    fresh[r] = valid[r] && !present[r];
-                }
-                __syncwarp();
+                    if (keep[r]) keep[r] = hash_insert(filt, fmask, fshift, c[r], err) != 0;
             }
 
-            uint32_t m = 0;
+            unsigned cnt = 0;
 #pragma unroll
             for (int r = 0; r < RY; ++r) {
-                const unsigned b = __ballot_sync(kFull, fresh[r]);
-                if (fresh[r]) {
-                    const uint32_t at = m + __popc(b & lt_mask);
-                    cids[at] = c[r];
-                    cpos[at] = static_cast<uint32_t>(r) * 32u + lane;
-                }
-                m += __popc(b);
+                const unsigned b = __ballot_sync(kFull, keep[r]);
+                if (keep[r]) ckeys[cnt + __popc(b & lt_mask)] = k[r];
+                cnt += __popc(b);
             }
-            __syncwarp();
-
-            if (m) {
-                filled += m;
-                D += m;
-                score_block<DM>(p, m, cpos, blk_rows, cdist, qsm, q8, lane, team_ok);
-                const uint64_t bound = beam_bound<RX>(beam, p.topk);
-                unsigned cnt = 0;
-#pragma unroll
-                for (int r = 0; r < RY; ++r) {
-                    const uint32_t s = static_cast<uint32_t>(r) * 32u + lane;
-                    const uint64_t k = s < m ? make_key(cdist[s], cids[s]) : kEmptyKey;
-                    const bool keep = k < bound;
-                    const unsigned b = __ballot_sync(kFull, keep);
-                    if (keep) ckeys[cnt + __popc(b & lt_mask)] = k;
-                    cnt += __popc(b);
-                }
-                if (cnt) {
-                    __syncwarp();
-                    beam_merge_compact<RX, RY>(beam, ckeys, cnt, lane, p.topk);
-                }
+            if (cnt) {
+                filled += cnt;
+                __syncwarp();
+                beam_merge_compact<RX, RY>(beam, ckeys, cnt, lane, p.topk);
             }
 
             if (FM == kBloom && p.reset_interval > 0 && (iter + 1) % p.reset_interval == 0) {
@@ -374,31 +382,47 @@ __global__ void __launch_bounds__(256) k_search_nb(const SearchParams p) {
     if (lane == 0 && err) atomicOr(&p.counters->error_flags, err);
 }
 
-// One warp per node: the node's adjacency row, then each neighbour's row
-// (zeros for an id outside the graph), 16 bytes per lane per step.
+// One warp per node: the node's adjacency row (a repeated id replaced by
+// kNoNode), then each neighbour's row (zeros for an id outside the graph),
+// 16 bytes per lane per step; u8 rows with their chunks rotated
+// (nb_chunk_pos).  Degree <= 64.
 __global__ void k_build_nb(const SearchParams p, unsigned char* __restrict__ out) {
     const unsigned lane = threadIdx.x & 31u;
     const uint64_t warp = (static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const uint64_t nwarps = (static_cast<uint64_t>(gridDim.x) * blockDim.x) >> 5;
-    const uint32_t src_bytes = p.vecs8 ? p.row_bytes : p.row_stride * 4u;
+    const bool u8 = p.vecs8 != nullptr;
+    const uint32_t src_bytes = u8 ? p.row_bytes : p.row_stride * 4u;
+    const uint32_t nch = src_bytes / 16u;
     const uint32_t chunks = p.nb_pitch / 16u;
+    const uint32_t deg = p.degree;
     for (uint64_t v = warp; v < p.n; v += nwarps) {
         unsigned char* dst = out + v * p.nb_stride;
-        const uint32_t* arow = p.adj + v * p.degree;
-        for (uint32_t i = lane; i < p.nb_adj_bytes / 4u; i += 32)
-            reinterpret_cast<uint32_t*>(dst)[i] = i < p.degree ? arow[i] : kNoNode;
-        const uint32_t total = p.degree * chunks;
+        const uint32_t* arow = p.adj + v * deg;
+        const uint32_t a0 = lane < deg ? arow[lane] : kNoNode;
+        const uint32_t a1 = lane + 32u < deg ? arow[lane + 32u] : kNoNode;
+        bool dup0 = false, dup1 = false;
+        for (uint32_t j = 0; j < deg; ++j) {
+            const uint32_t a = __shfl_sync(kFull, j < 32u ? a0 : a1, static_cast<int>(j & 31u));
+            dup0 |= j < lane && a == a0;
+            dup1 |= j < lane + 32u && a == a1;
+        }
+        uint32_t* dadj = reinterpret_cast<uint32_t*>(dst);
+        const uint32_t words = p.nb_adj_bytes / 4u;
+        if (lane < words) dadj[lane] = dup0 ? kNoNode : a0;
+        if (lane + 32u < words) dadj[lane + 32u] = dup1 ? kNoNode : a1;
+        const uint32_t total = deg * chunks;
         for (uint32_t t = lane; t < total; t += 32) {
             const uint32_t i = t / chunks, ch = t - i * chunks;
             const uint32_t child = arow[i];
             uint4 val = make_uint4(0u, 0u, 0u, 0u);
-            if (child < p.n && ch * 16u < src_bytes) {
-                const unsigned char* src = p.vecs8 ? p.vecs8 + static_cast<size_t>(child) * p.row_bytes
-                                                   : reinterpret_cast<const unsigned char*>(
-                                                         p.vecs + static_cast<size_t>(child) * p.row_stride);
+            if (child < p.n && ch < nch) {
+                const unsigned char* src = u8 ? p.vecs8 + static_cast<size_t>(child) * p.row_bytes
+                                              : reinterpret_cast<const unsigned char*>(
+                                                    p.vecs + static_cast<size_t>(child) * p.row_stride);
                 val = *reinterpret_cast<const uint4*>(src + ch * 16u);
             }
-            *reinterpret_cast<uint4*>(dst + p.nb_adj_bytes + static_cast<size_t>(i) * p.nb_pitch + ch * 16u) = val;
+            const uint32_t at = (u8 && ch < nch) ? nb_chunk_pos(ch, i, nch) : ch;
+            *reinterpret_cast<uint4*>(dst + p.nb_adj_bytes + static_cast<size_t>(i) * p.nb_pitch + at * 16u) = val;
         }
     }
 }
@@ -454,6 +478,7 @@ cudaError_t launch_search_nb(const SearchParams& p, const LaunchShape& shape, in
 }
 
 cudaError_t build_neighbourhood_blocks(const SearchParams& p, unsigned char* out, cudaStream_t stream) {
+    if (p.degree > 64u) return cudaErrorInvalidValue;
     const uint64_t warps = p.n;
     const uint64_t blocks64 = (warps + 7) / 8;
     const unsigned blocks = static_cast<unsigned>(blocks64 < 65535ull * 8 ? blocks64 : 65535ull * 8);

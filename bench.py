@@ -283,8 +283,10 @@ def run_ours(args, rank, world, local_rank):
     peak, peak_kind = peaks()
     achieved = alg_bytes / (statistics.mean(step_ms) / 1e3) / 1e9
     traffic = None
-    tp = os.path.join(ROOT, "profiles", "traffic_k_search_l2_c2.json")
-    if os.path.exists(tp):
+    # DRAM bytes of one launch of this kernel on this workload, from the ncu
+    # capture summarised in profiles/k_search_nb_c2.md
+    tp = os.path.join(ROOT, "profiles", "traffic_k_search_nb_c2.json")
+    if os.path.exists(tp) and st.block_bytes and chosen == 56:
         with open(tp) as f:
             traffic = json.load(f).get("dram_bytes_per_launch")
     line = {
