@@ -213,6 +213,43 @@ __device__ __forceinline__ bool beam_pick(uint64_t (&beam)[RX], unsigned lane, u
     return true;
 }
 
+// beam_pick that also returns the entry the next pick would take if the beam
+// did not change (kNoNode when there is none): a speculative prefetch target.
+template <int RX>
+__device__ __forceinline__ bool beam_pick_next(uint64_t (&beam)[RX], unsigned lane, uint32_t& node,
+                                               uint32_t& next) {
+    int sel = -1, sel2 = -1;
+    unsigned sel_mask = 0, sel2_mask = 0;
+#pragma unroll
+    for (int r = 0; r < RX; ++r) {
+        const bool open = beam[r] != kEmptyKey && (beam[r] & 1ull) == 0;
+        const unsigned m = __ballot_sync(kFull, open);
+        if (sel >= 0 && sel2 < 0 && m != 0) { sel2 = r; sel2_mask = m; }
+        if (sel < 0 && m != 0) { sel = r; sel_mask = m; }
+    }
+    if (sel < 0) return false;
+    const int src = __ffs(sel_mask) - 1;
+    const unsigned rest = sel_mask & (sel_mask - 1u);
+    int nreg = -1, nsrc = 0;
+    if (rest != 0) { nreg = sel; nsrc = __ffs(rest) - 1; }
+    else if (sel2 >= 0) { nreg = sel2; nsrc = __ffs(sel2_mask) - 1; }
+    uint32_t mine = 0, mine2 = 0;
+#pragma unroll
+    for (int r = 0; r < RX; ++r) {
+        if (r == sel) mine = static_cast<uint32_t>(beam[r]) >> 1;
+        if (r == nreg) mine2 = static_cast<uint32_t>(beam[r]) >> 1;
+    }
+    node = __shfl_sync(kFull, mine, src);
+    next = kNoNode;
+    if (nreg >= 0) next = __shfl_sync(kFull, mine2, nsrc);
+    if (static_cast<int>(lane) == src) {
+#pragma unroll
+        for (int r = 0; r < RX; ++r)
+            if (r == sel) beam[r] |= 1ull;
+    }
+    return true;
+}
+
 // ------------------------------------------------------------ filters
 
 // Exact visited set: linear probing on a power-of-two table of node ids

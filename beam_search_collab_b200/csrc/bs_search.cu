@@ -288,10 +288,10 @@ cudaError_t plan_search(SearchParams& p, LaunchShape& shape, size_t max_smem_opt
         // With neighbourhood blocks the table only holds ids that passed
         // into the beam, so it is sized to the beam instead of
         // filter_capacity (more resident warps).
-        const uint64_t want = p.nb != nullptr ? need : (p.filter_slots > need ? p.filter_slots : need);
+        const uint64_t want = p.nb != nullptr ? 4ull * (p.topk + p.degree) : (p.filter_slots > need ? p.filter_slots : need);
         const uint32_t slots = pow2_at_least(want);
         p.filter_slots = slots < 64 ? 64 : slots;
-        p.filter_limit = p.filter_slots / 4u * 3u;
+        p.filter_limit = p.nb != nullptr ? p.filter_slots / 4u : p.filter_slots / 4u * 3u;
         p.filter_words = p.filter_slots;
     } else {
         const uint32_t bits = pow2_at_least(p.filter_slots < 32 ? 32 : p.filter_slots);
@@ -307,15 +307,19 @@ cudaError_t plan_search(SearchParams& p, LaunchShape& shape, size_t max_smem_opt
     p.stage_pitch = (units % 2u == 0u) ? p.row_stride + 4u : p.row_stride + 8u;
     const uint32_t cand = 32u * static_cast<uint32_t>(shape.regy);
 
-    uint32_t off = align16(p.row_stride * 4u);
+    const bool blocks = p.nb != nullptr && p.codes == nullptr;
+    // the f32 query (the block kernel keeps it in global memory for byte rows)
+    uint32_t off = (blocks && shape.dmode == kU8) ? 0u : align16(p.row_stride * 4u);
     p.off_q8 = off;
     if (shape.dmode == kU8) off = align16(off + p.row_bytes + 4u);   // bytes + sum q^2
     p.off_filter = off;
     off = align16(off + p.filter_words * 4u);
-    p.off_cids = off;
-    off = align16(off + cand * 4u);
-    p.off_cdist = off;
-    off = align16(off + cand * 4u);
+    if (!blocks) {
+        p.off_cids = off;
+        off = align16(off + cand * 4u);
+        p.off_cdist = off;
+        off = align16(off + cand * 4u);
+    }
     p.off_keys = off;
     off = align16(off + cand * 8u);
     if (p.codes != nullptr) {
@@ -325,13 +329,16 @@ cudaError_t plan_search(SearchParams& p, LaunchShape& shape, size_t max_smem_opt
         off = align16(off + p.pdim * 4u + 7u * p.wpp * 4u);
     }
     p.off_stage = off;
-    if (p.nb != nullptr && p.codes == nullptr) {
+    if (blocks) {
         // neighbourhood blocks: the mbarrier and one block copy replace the
-        // staging area
+        // staging area; the entry's id and distance (the only users of
+        // cids/cdist) sit in the block buffer before its first copy
         p.off_mbar = off;
         off = align16(off + 8u);
         p.off_block = off;
-        off = align16(off + p.nb_stride);
+        p.off_cids = off;
+        p.off_cdist = off + 16u;
+        off = align16(off + (p.nb_stride > 32u ? p.nb_stride : 32u));
         p.stage_rows = 0;
     } else if (shape.dmode == kSeq) {
         const uint32_t row_bytes = p.stage_pitch * 4u;

@@ -68,6 +68,11 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, unsigned b
         : "memory");
 }
 
+// Hint: bring `bytes` at src into L2 (no completion to wait for).
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, unsigned bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(src), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* mbar, unsigned phase) {
     unsigned ok;
     asm volatile(
@@ -232,17 +237,21 @@ __global__ void __launch_bounds__(256) k_search_nb(const SearchParams p) {
         qi = __shfl_sync(kFull, qi, 0);
         if (qi >= p.nq) break;
 
+        // byte rows read the f32 query from global memory (packing, and the
+        // rare sequential fallback); the others keep it in shared memory
         const float* q = p.queries + static_cast<size_t>(qi) * p.dim;
-        for (uint32_t d = lane; d < p.row_stride; d += 32) qsm[d] = d < p.dim ? __ldg(q + d) : 0.0f;
+        const float* qv = DM == kU8 ? q : qsm;
+        if (DM != kU8)
+            for (uint32_t d = lane; d < p.row_stride; d += 32) qsm[d] = d < p.dim ? __ldg(q + d) : 0.0f;
         for (uint32_t i = lane; i < p.filter_words; i += 32) filt[i] = (FM == kHash) ? kNoNode : 0u;
         if (lane == 0) cids[0] = p.entry;
         __syncwarp();
-        const bool team_ok = DM != kSeq && query_integer_exact(qsm, p.dim, p.team_qlo, p.team_qhi);
+        const bool team_ok = DM != kSeq && query_integer_exact(qv, p.dim, p.team_qlo, p.team_qhi);
         if (DM != kSeq && !team_ok && lane == 0) atomicAdd(&p.counters->team_fallbacks, 1u);
-        if (DM == kU8 && team_ok) pack_query_u8(qsm, p.dim, p.row_bytes, q8, lane);
+        if (DM == kU8 && team_ok) pack_query_u8(qv, p.dim, p.row_bytes, q8, lane);
         const uint32_t qq = (DM == kU8 && team_ok) ? q8[p.row_bytes / 4u] : 0u;
 
-        score_direct<DM>(p, 1, cids, cdist, qsm, q8, lane, team_ok);
+        score_direct<DM>(p, 1, cids, cdist, qv, q8, lane, team_ok);
         uint64_t beam[RX];
 #pragma unroll
         for (int r = 0; r < RX; ++r) beam[r] = kEmptyKey;
@@ -253,15 +262,23 @@ __global__ void __launch_bounds__(256) k_search_nb(const SearchParams p) {
         }
         uint32_t filled = 1;
         uint32_t E = 0, D = 1;
+        // cids/cdist of the entry live in the block buffer: order these
+        // generic accesses before the first bulk copy overwrites them
+        asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
         __syncwarp();
 
         for (int iter = 0; iter < p.max_iterations; ++iter) {
-            uint32_t cur;
-            if (!beam_pick<RX>(beam, lane, cur)) break;
+            uint32_t cur, nxt;
+            if (!beam_pick_next<RX>(beam, lane, cur, nxt)) break;
             ++E;
             __syncwarp();   // earlier reads of the block and of ckeys are done
 
-            if (lane == 0) bulk_load(blk, p.nb + static_cast<size_t>(cur) * p.nb_stride, p.nb_stride, mbar);
+            if (lane == 0) {
+                bulk_load(blk, p.nb + static_cast<size_t>(cur) * p.nb_stride, p.nb_stride, mbar);
+                // the block the next expansion takes unless a better
+                // candidate turns up: start it towards L2 now
+                if (nxt != kNoNode) bulk_prefetch_l2(p.nb + static_cast<size_t>(nxt) * p.nb_stride, p.nb_stride);
+            }
             if (!mbar_wait(mbar, phase)) {
                 // give the copy in flight a last bounded chance, then leave:
                 // the host reads the flag and reports BS_ERR_KERNEL
@@ -302,7 +319,7 @@ __global__ void __launch_bounds__(256) k_search_nb(const SearchParams p) {
             for (int r = 0; r < RY; ++r) {
                 float d = 0.0f;
                 if (live[r])
-                    d = block_row_dist<DM>(p, blk_rows, static_cast<uint32_t>(r) * 32u + lane, qsm, qb, qq, team_ok);
+                    d = block_row_dist<DM>(p, blk_rows, static_cast<uint32_t>(r) * 32u + lane, qv, qb, qq, team_ok);
                 k[r] = live[r] ? make_key(d, c[r]) : kEmptyKey;
                 D += __popc(__ballot_sync(kFull, live[r]));
                 keep[r] = k[r] < bound;
