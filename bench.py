@@ -300,7 +300,9 @@ def run_ours(args, rank, world, local_rank):
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "f32",
+        # rows stored as bytes (128 B for the 128-d C2 rows): u8 products
+        # summed exactly in int32 with __dp4a
+        "dtype": "u8" if st.integer_exact and st.row_bytes == 128 else "f32",
         "data": "synthetic: seeded C2 mixture (1,024 Gaussians, ints 0..255), graph from the reference build_graph settings",
         "config": {
             "workload": "C2: 1M x 128 int-valued base, 10k queries per GPU, degree-32 Vamana, K=10",
