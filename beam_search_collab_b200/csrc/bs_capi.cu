@@ -107,6 +107,19 @@ bool is_device_ptr(const void* ptr) {
     return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
 }
 
+// Page-locked host memory that `device`'s context has mapped: the device
+// address its kernels read and write it through, else null (pageable memory,
+// or pinned by another device's context).
+void* mapped_host_ptr(const void* ptr, int device) {
+    if (!ptr) return nullptr;
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, ptr) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    return (a.type == cudaMemoryTypeHost && a.device == device) ? a.devicePointer : nullptr;
+}
+
 struct ModeInfo {
     bool rabitq = false;
     bsb::FilterMode fmode = bsb::kHash;
@@ -580,15 +593,25 @@ BS_API bs_status bs_search(bs_index* ix, const bs_search_params* prm, const floa
     const bool q_dev = is_device_ptr(queries);
     const bool i_dev = is_device_ptr(ids);
     const bool d_dev = dists ? is_device_ptr(dists) : true;
+    // Host buffers that are page-locked and mapped into this device's
+    // context are used in place: each warp reads its query over the bus when
+    // it starts it and writes its result row back when it ends, so the
+    // transfers overlap the search instead of bracketing it.  Pageable
+    // buffers go through device staging and whole-batch copies.
+    const float* q_map = q_dev ? nullptr : static_cast<const float*>(mapped_host_ptr(queries, ix->device));
+    uint32_t* i_map = i_dev ? nullptr : static_cast<uint32_t*>(mapped_host_ptr(ids, ix->device));
+    float* d_map = d_dev ? nullptr : static_cast<float*>(mapped_host_ptr(dists, ix->device));
+    const bool i_stage = !i_dev && !i_map;
+    const bool d_stage = dists && !d_dev && !d_map;
     const size_t qbytes = static_cast<size_t>(nq) * ix->dim * sizeof(float);
     const size_t obytes = static_cast<size_t>(nq) * p.K * sizeof(uint32_t);
     size_t off = 256;   // DevCounters at 0
     const size_t q_off = off;
-    if (!q_dev) off += (qbytes + 255) & ~static_cast<size_t>(255);
+    if (!q_dev) off += (qbytes + 255) & ~static_cast<size_t>(255);   // staging, or the kernel's query slots
     const size_t i_off = off;
-    if (!i_dev) off += (obytes + 255) & ~static_cast<size_t>(255);
+    if (i_stage) off += (obytes + 255) & ~static_cast<size_t>(255);
     const size_t d_off = off;
-    if (dists && !d_dev) off += (obytes + 255) & ~static_cast<size_t>(255);
+    if (d_stage) off += (obytes + 255) & ~static_cast<size_t>(255);
     const size_t s_off = off;
     if (mi.rabitq) {
         uint64_t warps = 0;
@@ -603,12 +626,13 @@ BS_API bs_status bs_search(bs_index* ix, const bs_search_params* prm, const floa
     auto release = [&]() { cudaFreeAsync(scratch, stream); };
     p.counters = reinterpret_cast<DevCounters*>(scratch);
     p.queries = q_dev ? queries : reinterpret_cast<const float*>(scratch + q_off);
-    p.out_ids = i_dev ? ids : reinterpret_cast<uint32_t*>(scratch + i_off);
-    p.out_dists = dists ? (d_dev ? dists : reinterpret_cast<float*>(scratch + d_off)) : nullptr;
+    p.queries_src = q_map;
+    p.out_ids = i_dev ? ids : i_map ? i_map : reinterpret_cast<uint32_t*>(scratch + i_off);
+    p.out_dists = !dists ? nullptr : d_dev ? dists : d_map ? d_map : reinterpret_cast<float*>(scratch + d_off);
     p.spill = mi.rabitq ? reinterpret_cast<uint32_t*>(scratch + s_off) : nullptr;
 
     e = cudaMemsetAsync(scratch, 0, sizeof(DevCounters), stream);
-    if (e == cudaSuccess && !q_dev)
+    if (e == cudaSuccess && !q_dev && !q_map)
         e = cudaMemcpyAsync(scratch + q_off, queries, qbytes, cudaMemcpyHostToDevice, stream);
     if (e != cudaSuccess) { release(); return cuda_fail(e, "query upload"); }
 
@@ -617,8 +641,8 @@ BS_API bs_status bs_search(bs_index* ix, const bs_search_params* prm, const floa
                   : bsb::launch_search(p, shape, ix->num_sms, stream);
     if (e != cudaSuccess) { release(); return cuda_fail(e, "search launch"); }
 
-    if (!i_dev) e = cudaMemcpyAsync(ids, scratch + i_off, obytes, cudaMemcpyDeviceToHost, stream);
-    if (e == cudaSuccess && dists && !d_dev)
+    if (i_stage) e = cudaMemcpyAsync(ids, scratch + i_off, obytes, cudaMemcpyDeviceToHost, stream);
+    if (e == cudaSuccess && d_stage)
         e = cudaMemcpyAsync(dists, scratch + d_off, obytes, cudaMemcpyDeviceToHost, stream);
     DevCounters hc{};
     const bool sync = stats || !q_dev || !i_dev || !d_dev;

@@ -81,6 +81,10 @@ struct SearchParams {
     uint32_t wpp;
     // queries
     const float* queries;       // [nq][dim] (stride dim)
+    // the caller's pinned host queries through their device mapping: read
+    // once per query over the bus (then `queries` is a device slot array the
+    // kernel may fill), or null when `queries` already holds them
+    const float* queries_src;
     uint32_t nq;
     // search config
     uint32_t topk;              // beam size T (topk_size)

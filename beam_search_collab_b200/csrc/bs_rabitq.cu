@@ -69,8 +69,8 @@ __global__ void __launch_bounds__(256) k_search_rabitq(const SearchParams p) {
         qi = __shfl_sync(kFull, qi, 0);
         if (qi >= p.nq) break;
 
-        const float* q = p.queries + static_cast<size_t>(qi) * p.dim;
-        for (uint32_t d = lane; d < p.row_stride; d += 32) qsm[d] = d < p.dim ? __ldg(q + d) : 0.0f;
+        const float* q = query_src(p, qi);
+        for (uint32_t d = lane; d < p.row_stride; d += 32) qsm[d] = d < p.dim ? q[d] : 0.0f;
         for (uint32_t i = lane; i < p.filter_words; i += 32) filt[i] = kNoNode;
         __syncwarp();
         const bool team_ok = DM != kSeq && query_integer_exact(qsm, p.dim, p.team_qlo, p.team_qhi);

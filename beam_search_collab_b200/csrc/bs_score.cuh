@@ -8,6 +8,13 @@
 namespace bsb {
 namespace dev {
 
+// Where query qi is read from: the caller's pinned host buffer through its
+// device mapping (plain loads, once per query, over the bus), else the
+// device array.
+__device__ __forceinline__ const float* query_src(const SearchParams& p, uint32_t qi) {
+    return (p.queries_src != nullptr ? p.queries_src : p.queries) + static_cast<size_t>(qi) * p.dim;
+}
+
 // Whole-warp test of the integer-exact condition for the query in smem:
 // every value an integer in [qlo, qhi].  The host derives that range from the
 // base vectors' own range so that every |q_d - x_d| <= B with

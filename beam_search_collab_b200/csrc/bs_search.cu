@@ -57,8 +57,8 @@ __global__ void __launch_bounds__(256) k_search_l2(const SearchParams p) {
         if (qi >= p.nq) break;
 
         // query -> shared memory (zero pad up to the stored row width)
-        const float* q = p.queries + static_cast<size_t>(qi) * p.dim;
-        for (uint32_t d = lane; d < p.row_stride; d += 32) qsm[d] = d < p.dim ? __ldg(q + d) : 0.0f;
+        const float* q = query_src(p, qi);
+        for (uint32_t d = lane; d < p.row_stride; d += 32) qsm[d] = d < p.dim ? q[d] : 0.0f;
         for (uint32_t i = lane; i < p.filter_words; i += 32) filt[i] = (FM == kHash) ? kNoNode : 0u;
         if (lane == 0) cids[0] = p.entry;
         __syncwarp();

@@ -239,10 +239,17 @@ __global__ void __launch_bounds__(256) k_search_nb(const SearchParams p) {
 
         // byte rows read the f32 query from global memory (packing, and the
         // rare sequential fallback); the others keep it in shared memory
-        const float* q = p.queries + static_cast<size_t>(qi) * p.dim;
+        const float* q = query_src(p, qi);
+        if (DM == kU8 && p.queries_src != nullptr) {
+            // read over the bus once, into this query's device slot
+            float* slot = const_cast<float*>(p.queries) + static_cast<size_t>(qi) * p.dim;
+            for (uint32_t d = lane; d < p.dim; d += 32) slot[d] = q[d];
+            __syncwarp();
+            q = slot;
+        }
         const float* qv = DM == kU8 ? q : qsm;
         if (DM != kU8)
-            for (uint32_t d = lane; d < p.row_stride; d += 32) qsm[d] = d < p.dim ? __ldg(q + d) : 0.0f;
+            for (uint32_t d = lane; d < p.row_stride; d += 32) qsm[d] = d < p.dim ? q[d] : 0.0f;
         for (uint32_t i = lane; i < p.filter_words; i += 32) filt[i] = (FM == kHash) ? kNoNode : 0u;
         if (lane == 0) cids[0] = p.entry;
         __syncwarp();

@@ -197,6 +197,46 @@ def test_device_and_host_buffers_agree(indexes):
     assert np.array_equal(d_d.cpu().numpy(), d_h)
 
 
+@pytest.mark.parametrize("name,mode,topk", [("i128", "warp4", 64), ("f48", "bwarp2", 64), ("s96d64", "rabitq", 128)])
+@pytest.mark.parametrize("host", ["pageable", "pinned"])
+def test_large_host_batch_matches_device_batch_and_golden_rows(indexes, name, mode, topk, host):
+    """Host buffers reach the kernels two ways: pageable memory through device
+    staging and whole-batch copies, page-locked memory in place (each warp
+    reads its query over the bus and writes its result row back).  Both must
+    give the device-buffer result row for row.  The batch repeats the golden
+    queries, so each copy of a query returns the same row, the first the
+    golden one."""
+    torch = pytest.importorskip("torch")
+    g, ix = indexes[name]
+    if mode == "rabitq" and not g.codebook_path:
+        pytest.skip("codebook not available")
+    reps = -(-9000 // len(g.queries))
+    q = np.ascontiguousarray(np.tile(g.queries, (reps, 1))[:9000])
+    kw = dict(mode=mode, K=10, topk_size=topk)
+    if host == "pageable":
+        ids_h, d_h, st_h = ix.search(q, **kw)
+    else:
+        hq = torch.from_numpy(q).pin_memory()
+        hid = torch.full((len(q), 10), 7, dtype=torch.int32).pin_memory()
+        hd = torch.zeros((len(q), 10), dtype=torch.float32).pin_memory()
+        st_h = B.Stats()
+        ix.search_raw(hq.data_ptr(), len(q), hid.data_ptr(), hd.data_ptr(), B.SearchParams(**kw), stats=st_h)
+        ids_h, d_h = hid.numpy().view(np.uint32), hd.numpy()
+    ids_d, d_d, st_d = ix.search(torch.from_numpy(q).cuda(), **kw)
+    torch.cuda.synchronize()
+    assert np.array_equal(ids_d.cpu().numpy().view(np.uint32), ids_h)
+    assert np.array_equal(d_d.cpu().numpy().view(np.uint32), d_h.view(np.uint32))
+    assert st_h.expansions == st_d.expansions and st_h.distances == st_d.distances
+    assert st_h.error_flags == 0
+    nq0 = len(g.queries)
+    for r in range(1, reps):
+        n = min(nq0, len(q) - r * nq0)
+        assert np.array_equal(ids_h[r * nq0:r * nq0 + n], ids_h[:n])
+    if mode != "bwarp2":
+        exp, _ = g.expected("rabitq" if mode == "rabitq" else "base", 10, topk)
+        assert (ids_h[:nq0] == exp).all()
+
+
 def test_k_larger_than_beam_pads_with_no_node(indexes):
     g, ix = indexes["f48"]
     ids, dists, _ = ix.search(g.queries[:8], mode="warp1", K=80, topk_size=32)
