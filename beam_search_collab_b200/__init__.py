@@ -69,7 +69,8 @@ class Stats(ctypes.Structure):
 # Every symbol include/bsearch.h declares (checked by the CPU test suite).
 EXPORTS = ("bs_search_params_default", "bs_index_create", "bs_index_load", "bs_index_attach_rabitq",
            "bs_index_load_codebook", "bs_index_info", "bs_index_entry_point", "bs_index_rabitq_entry",
-           "bs_index_destroy", "bs_search", "bs_search_no_alloc", "bs_device_alloc", "bs_device_free",
+           "bs_index_destroy", "bs_search", "bs_search_no_alloc", "bs_merge_shards", "bs_device_alloc",
+           "bs_device_free",
            "bs_copy_to_device",
            "bs_copy_to_host", "bs_device_fill", "bs_synchronize", "bs_last_error", "bs_version")
 
@@ -101,6 +102,9 @@ def lib() -> ctypes.CDLL:
                             ctypes.POINTER(Stats), vp]
     L.bs_search_no_alloc.argtypes = [vp, ctypes.POINTER(_Params), vp, ctypes.c_uint32, vp, vp, vp]
     L.bs_search_no_alloc.restype = st
+    L.bs_merge_shards.argtypes = [vp, vp, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, _u32p,
+                                  ctypes.c_uint32, vp, vp, vp]
+    L.bs_merge_shards.restype = st
     L.bs_device_alloc.argtypes = [vp, ctypes.c_size_t, ctypes.POINTER(vp)]
     L.bs_device_free.argtypes = [vp, vp]
     L.bs_copy_to_device.argtypes = [vp, vp, vp, ctypes.c_size_t]
@@ -246,6 +250,25 @@ class Index:
                                ctypes.c_void_p(ids_ptr), ctypes.c_void_p(dists_ptr or None),
                                ctypes.byref(stats) if stats is not None else None,
                                ctypes.c_void_p(stream or None)))
+
+
+def merge_shards(dists, ids, id_offsets, K_out: int, stream: int = 0):
+    """bs_merge_shards on CUDA tensors: dists float32 [S, nq, K], ids int32
+    [S, nq, K] (shard-local ids, -1 = none), one id offset per shard.
+    Returns (ids [nq, K_out] int32 with global ids, dists [nq, K_out])."""
+    import torch
+    if not (dists.is_contiguous() and ids.is_contiguous()):
+        raise ValueError("merge_shards needs contiguous tensors")
+    S, nq, K = ids.shape
+    out_ids = torch.empty((nq, K_out), dtype=torch.int32, device=ids.device)
+    out_d = torch.empty((nq, K_out), dtype=torch.float32, device=ids.device)
+    offs = (ctypes.c_uint32 * S)(*[int(o) for o in id_offsets])
+    import contextlib
+    with torch.cuda.device(ids.device) if ids.is_cuda else contextlib.nullcontext():
+        _check(lib().bs_merge_shards(ctypes.c_void_p(_ptr(dists)), ctypes.c_void_p(_ptr(ids)), S, nq, K, offs,
+                                     K_out, ctypes.c_void_p(_ptr(out_ids)), ctypes.c_void_p(_ptr(out_d)),
+                                     ctypes.c_void_p(stream or None)))
+    return out_ids, out_d
 
 
 def run_cli(config: dict, timeout: float = 600) -> subprocess.CompletedProcess:

@@ -27,7 +27,7 @@ BIN_DIR = os.path.join(PKG, "bin")
 LIB = os.path.join(LIB_DIR, "libbsearch_b200.so")
 CLI = os.path.join(BIN_DIR, "gpu_cli")
 
-CU_SOURCES = ["bs_search.cu", "bs_search_nb.cu", "bs_rabitq.cu", "bs_entry.cu", "bs_capi.cu"]
+CU_SOURCES = ["bs_search.cu", "bs_search_nb.cu", "bs_rabitq.cu", "bs_entry.cu", "bs_merge.cu", "bs_capi.cu"]
 NVCC_FLAGS = ["-std=c++17", "-O3", "-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo",
               "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
               "--ptxas-options=--warn-on-local-memory-usage"]

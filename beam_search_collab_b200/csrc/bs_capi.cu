@@ -793,6 +793,37 @@ BS_API bs_status bs_search_no_alloc(bs_index* ix, const bs_search_params* prm, c
     return BS_OK;
 }
 
+BS_API bs_status bs_merge_shards(const float* dists, const uint32_t* ids, uint32_t shards, uint32_t nq,
+                                 uint32_t K, const uint32_t* id_offsets, uint32_t K_out, uint32_t* out_ids,
+                                 float* out_dists, void* stream) {
+    if (shards == 0 || shards > bsb::kMaxShards)
+        return fail(BS_ERR_INVALID_ARGUMENT, "shards must be in 1..%u", bsb::kMaxShards);
+    if (K == 0 || K_out == 0 || K_out > static_cast<uint64_t>(shards) * K)
+        return fail(BS_ERR_INVALID_ARGUMENT, "need 0 < K_out <= shards * K");
+    if (!id_offsets) return fail(BS_ERR_INVALID_ARGUMENT, "id_offsets is NULL");
+    if (nq == 0) return BS_OK;
+    if (!is_device_ptr(dists) || !is_device_ptr(ids) || !is_device_ptr(out_ids) ||
+        (out_dists && !is_device_ptr(out_dists)))
+        return fail(BS_ERR_INVALID_ARGUMENT, "bs_merge_shards takes device pointers");
+    int dev = 0, sms = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return cuda_fail(e, "device query");
+    bsb::MergeArgs a{};
+    a.dists = dists;
+    a.ids = ids;
+    a.shards = shards;
+    a.nq = nq;
+    a.K = K;
+    a.K_out = K_out;
+    for (uint32_t s = 0; s < shards; ++s) a.offsets[s] = id_offsets[s];
+    a.out_ids = out_ids;
+    a.out_dists = out_dists;
+    e = bsb::launch_merge_shards(a, sms, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "merge launch");
+    return BS_OK;
+}
+
 BS_API bs_status bs_device_alloc(const bs_index* ix, size_t bytes, void** dptr) {
     if (!ix || !dptr) return fail(BS_ERR_INVALID_ARGUMENT, "index or dptr is NULL");
     DeviceGuard g(ix->device);

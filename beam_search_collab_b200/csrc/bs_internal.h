@@ -152,6 +152,18 @@ cudaError_t build_neighbourhood_blocks(const SearchParams& p, unsigned char* out
 cudaError_t rabitq_grid_warps(const SearchParams& p, const LaunchShape& shape, int num_sms,
                               uint64_t& warps);
 
+// Merge of per-shard result lists (bs_merge.cu).
+constexpr uint32_t kMaxShards = 32;
+struct MergeArgs {
+    const float* dists;          // [shards][nq][K], each list ascending
+    const uint32_t* ids;         // [shards][nq][K], shard-local ids, 0xffffffff = none
+    uint32_t shards, nq, K, K_out;
+    uint32_t offsets[kMaxShards];  // global id = local id + offsets[shard]
+    uint32_t* out_ids;           // [nq][K_out]
+    float* out_dists;            // [nq][K_out] or null
+};
+cudaError_t launch_merge_shards(const MergeArgs& a, int num_sms, cudaStream_t stream);
+
 // Entry point (bs_entry.cu): centroid-nearest row, reference arithmetic, over
 // f32 rows (vecs) or exact u8 rows (vecs8, row stride in bytes).
 cudaError_t compute_entry_point(const float* vecs, uint64_t n, uint32_t dim, uint32_t row_stride,

@@ -128,8 +128,11 @@ BS_API void bs_index_destroy(bs_index* index);
  * (src/gpu_cli.cu:87-349): searches nq queries ([nq][dim] floats), writes
  * ids [nq][K] (BS_NO_NODE past the end of the beam) and, when `dists` is not
  * NULL, the matching squared L2 distances.  `queries`, `ids` and `dists` may
- * each be host or device pointers; host buffers are copied inside the call,
- * which then returns only when the results are in place.  With device
+ * each be host or device pointers.  Pageable host buffers are copied inside
+ * the call; page-locked host buffers mapped into the index's device (e.g.
+ * cudaHostAlloc / cudaMallocHost on that device) are read and written in
+ * place by the search kernel, so their transfers overlap the search.  With
+ * any host buffer the call returns only when the results are in place.  With device
  * buffers only and stats == NULL the call is asynchronous on `stream`
  * (a cudaStream_t; NULL = legacy default stream). */
 BS_API bs_status bs_search(bs_index* index, const bs_search_params* params, const float* queries,
@@ -160,6 +163,21 @@ BS_API bs_status bs_search(bs_index* index, const bs_search_params* params, cons
  *   - asynchronous on `stream`; no statistics are returned. */
 BS_API bs_status bs_search_no_alloc(bs_index* index, const bs_search_params* params, const float* queries,
                                     uint32_t nq, uint32_t* ids, float* dists, void* stream);
+
+/* No counterpart in the reference, which searches one index on one GPU: the
+ * merge step of a sharded index (one shard per GPU, each with its own graph
+ * over its own rows; every query searched on every shard).  Input: the
+ * shards' result lists gathered into dists[shards][nq][K] and
+ * ids[shards][nq][K] (shard-local ids, BS_NO_NODE past the end, each list
+ * ascending by (distance, id) as bs_search returns it), device pointers on
+ * the current device.  Output: out_ids[nq][K_out] (and out_dists when not
+ * NULL), the K_out smallest (distance, global id) entries over all shards,
+ * global id = local id + id_offsets[shard] (a host array of `shards` values;
+ * global ids must stay below 0xffffffff), BS_NO_NODE / FLT_MAX past the end.
+ * shards <= 32, K_out <= shards * K.  Asynchronous on `stream`. */
+BS_API bs_status bs_merge_shards(const float* dists, const uint32_t* ids, uint32_t shards, uint32_t nq,
+                                 uint32_t K, const uint32_t* id_offsets, uint32_t K_out, uint32_t* out_ids,
+                                 float* out_dists, void* stream);
 
 /* Device buffers on the index's device (for callers that stage queries once
  * and search many times, like the reference CLI's timed loop,
