@@ -85,7 +85,7 @@ def _nccl_rank(rank, world, port, out):
 def test_sharded_index_over_nccl_matches_reference_merge():
     import torch.multiprocessing as mp
     world = 2
-    with mp.Manager() as m:
+    with mp.get_context("spawn").Manager() as m:
         out = m.dict()
         mp.start_processes(_nccl_rank, args=(world, _free_port(), out), nprocs=world, start_method="spawn")
         res = dict(out)

@@ -52,7 +52,7 @@ def _rank(rank, world, port, K, topk, out):
 def test_two_gloo_ranks_exchange_and_merge_shard_results():
     world, K, topk = 2, 10, 32
     port = _free_port()
-    with mp.Manager() as m:
+    with mp.get_context("spawn").Manager() as m:
         out = m.dict()
         mp.start_processes(_rank, args=(world, port, K, topk, out), nprocs=world, start_method="spawn")
         res = dict(out)
