@@ -459,6 +459,10 @@ def main():
     if world > 1 and args.impl == "ours":
         import datetime
         import torch
+        # stdout carries exactly one JSON line: keep NCCL's version banner off
+        # it unless more NCCL logging was asked for
+        if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
+            os.environ["NCCL_DEBUG"] = "WARN"
         torch.cuda.set_device(local_rank)
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
                                              device_id=torch.device("cuda", local_rank))
