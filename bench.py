@@ -450,7 +450,7 @@ def main():
     args = ap.parse_args()
     if args.profile_run:
         profile_run(args)
-        return
+        return None, 0
     args.warmup = max(args.warmup, 3)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -459,10 +459,6 @@ def main():
     if world > 1 and args.impl == "ours":
         import datetime
         import torch
-        # stdout carries exactly one JSON line: keep NCCL's version banner off
-        # it unless more NCCL logging was asked for
-        if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
-            os.environ["NCCL_DEBUG"] = "WARN"
         torch.cuda.set_device(local_rank)
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
                                              device_id=torch.device("cuda", local_rank))
@@ -470,12 +466,23 @@ def main():
         line = run_reference(args, rank, world)
     else:
         line = run_ours(args, rank, world, local_rank)
-    if rank == 0 and line is not None:
-        print(json.dumps(line), flush=True)
     if world > 1 and args.impl == "ours":
         import torch
         torch.distributed.destroy_process_group()
+    return line, rank
 
 
 if __name__ == "__main__":
-    main()
+    # stdout carries exactly one JSON line: while the run goes, file
+    # descriptor 1 points at stderr (libraries such as NCCL print to stdout)
+    sys.stdout.flush()
+    _stdout_fd = os.dup(1)
+    os.dup2(2, 1)
+    try:
+        _line, _rank = main()
+    finally:
+        sys.stdout.flush()
+        os.dup2(_stdout_fd, 1)
+        os.close(_stdout_fd)
+    if _rank == 0 and _line is not None:
+        print(json.dumps(_line), flush=True)
