@@ -8,6 +8,12 @@ recall@10 against the exact top-10 is >= 0.95; a "step" is one search of all
 of a GPU's queries at that point.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config c2|c3|c4]
+
+--config selects another BASELINE.json workload for measurement (default and
+the driver's line: c2): c3 = RaBitQ search (1M x 96 unit vectors, degree 64,
+the reference build_rabitq codebook), c4 = 960-d exact search (1k queries,
+K 100, topk 256).  Their graphs and codebooks live in bench_data/<config>/.
 
 Arms
   ours       : the CUDA search through the C ABI (lib/libbsearch_b200.so).
@@ -49,6 +55,46 @@ TARGET_RECALL = 0.95
 K = 10
 NQ_PER_GPU = 10_000
 FLUSH_BYTES = 256 << 20
+# topk_size at which the C2 search first reaches recall@10 >= 0.95 (the sweep
+# of the GPU arm finds it; the CPU reference arm, which cannot afford the
+# ground truth, searches at the same point)
+C2_OPERATING_TOPK = 56
+
+# Workloads.  The driver's bench line is C2; C3 and
+# C4 measure the RaBitQ path and the 960-d gather path with --config.
+CONFIGS = {
+    "c2": dict(gen="gen_c2", nq=10_000, mode="warp4", K=10, sweep=TOPK_SWEEP, codebook=False,
+               operating_topk=C2_OPERATING_TOPK,
+               workload="C2: 1M x 128 int-valued base, 10k queries per GPU, degree-32 Vamana, K=10",
+               data="synthetic: seeded C2 mixture (1,024 Gaussians, ints 0..255), graph from the "
+                    "reference build_graph settings"),
+    "c3": dict(gen="gen_c3", nq=10_000, mode="rabitq", K=10, sweep=(128, 160, 192, 256, 384, 512), codebook=True,
+               workload="C3: 1M x 96 unit-norm base, 10k queries per GPU, degree-64 Vamana, RaBitQ codebook "
+                        "(build_rabitq seed 12345), K=10, exact rerank",
+               data="synthetic: seeded C3 mixture (256 clusters on the unit sphere, concentration 20), graph "
+                    "and codebook from the reference build_graph / build_rabitq"),
+    "c4": dict(gen="gen_c4", nq=1_000, mode="base", K=100, sweep=(256,), codebook=False,
+               workload="C4: 1M x 960 non-negative base, 1k queries per GPU, degree-32 Vamana, K=100, topk 256",
+               data="synthetic: seeded C4 (|N(0,1)| * 0.1 * per-dimension log-uniform scale), graph from the "
+                    "reference build_graph settings"),
+}
+CFG_NAME = "c2"
+
+
+def config_data(name: str, nq_total: int):
+    """Base, queries, graph edges and codebook path (or None) of a workload;
+    graphs and codebooks are built once with the reference tools into
+    bench_data/<config>/ (git-ignored, shipped to the GPU box)."""
+    from beam_search_collab_b200 import datasets as ds
+    cfg = CONFIGS[name]
+    s = getattr(ds, cfg["gen"])(nq=nq_total)
+    graph = os.path.join(DATA_DIR, name, "graph.bin")
+    if not os.path.exists(graph):
+        raise SystemExit(f"missing {graph}: build it with the reference build_graph over the {name} base")
+    cb = os.path.join(DATA_DIR, name, "codebook.bin") if cfg["codebook"] else None
+    if cb and not os.path.exists(cb):
+        raise SystemExit(f"missing {cb}: build it with the reference build_rabitq (-seed 12345)")
+    return s.base, s.queries, ds.read_graph(graph), cb
 
 
 # ------------------------------------------------------------------ helpers
@@ -176,22 +222,26 @@ def run_ours(args, rank, world, local_rank):
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
+    cfg = CONFIGS[CFG_NAME]
     t0 = time.time()
-    base, queries_all = c2_data(NQ_PER_GPU * world)
+    base, queries_all, edges, codebook = config_data(CFG_NAME, NQ_PER_GPU * world)
     queries = queries_all[rank * NQ_PER_GPU:(rank + 1) * NQ_PER_GPU]
-    edges = load_graph()
     log(f"[rank {rank}] data ready in {time.time() - t0:.1f}s: base {base.shape}, graph {edges.shape}")
     ix = B.Index.from_arrays(base, edges, device=local_rank)
-    entry = ix.entry_point()
+    if codebook:
+        ix.load_codebook(codebook)
+    entry = ix.rabitq_entry() if args.mode == "rabitq" else B.NO_NODE
+    if entry == B.NO_NODE:
+        entry = ix.entry_point()
 
     base_t = torch.from_numpy(base).to(dev)
     q_std = torch.from_numpy(queries_all[:NQ_PER_GPU]).to(dev)
-    gt = gpu_ground_truth(base_t, q_std, K)
+    gt = gpu_ground_truth(base_t, q_std, 10)
     del base_t
 
     # operating point: smallest beam reaching the recall target (same on every rank)
     chosen, sweep = None, []
-    for T in ([args.topk] if args.topk else TOPK_SWEEP):
+    for T in ([args.topk] if args.topk else cfg["sweep"]):
         ids, _, st = ix.search(q_std, mode=args.mode, K=K, topk_size=T)
         torch.cuda.synchronize()
         r = recall_at_k(ids.cpu().numpy().astype(np.int64), gt)
@@ -213,7 +263,14 @@ def run_ours(args, rank, world, local_rank):
     # query read + per expansion either one neighbourhood block (adjacency row
     # and all neighbour rows, copied whole) or the adjacency row and the rows of
     # the scored candidates as stored (u8 copy: 1 B/dim) + ids and distances
-    if st.block_bytes:
+    if args.mode == "rabitq":
+        # per expansion: adjacency row, the neighbours' 1-bit codes (pdim/8 B
+        # each) and 3 f32 factors each, and the parent's exact row; then the
+        # exact rerank rows of the final beam
+        pdim = 1 << (dim - 1).bit_length()
+        per_expansion = (st.expansions * (4 * deg + deg * pdim // 8 + 12 * deg + st.row_bytes)
+                         + st.rerank * st.row_bytes)
+    elif st.block_bytes:
         per_expansion = st.expansions * st.block_bytes
     else:
         per_expansion = st.expansions * 4 * deg + st.distances * st.row_bytes
@@ -285,10 +342,13 @@ def run_ours(args, rank, world, local_rank):
     traffic = None
     # DRAM bytes of one launch of this kernel on this workload, from the ncu
     # capture summarised in profiles/k_search_nb_c2.md
-    tp = os.path.join(ROOT, "profiles", "traffic_k_search_nb_c2.json")
-    if os.path.exists(tp) and st.block_bytes and chosen == 56:
+    tp = os.path.join(ROOT, "profiles", f"traffic_{CFG_NAME}.json")
+    if os.path.exists(tp):
         with open(tp) as f:
-            traffic = json.load(f).get("dram_bytes_per_launch")
+            tj = json.load(f)
+        if tj.get("topk_size") == chosen and tj.get("mode") == args.mode and tj.get("layout") == (
+                "blocks" if st.block_bytes else "gather"):
+            traffic = tj.get("dram_bytes_per_launch")
     line = {
         "metric": "QPS at recall@10>=0.95",
         "value": round(value, 1),
@@ -302,10 +362,10 @@ def run_ours(args, rank, world, local_rank):
         "vs_baseline": None,
         # rows stored as bytes (128 B for the 128-d C2 rows): u8 products
         # summed exactly in int32 with __dp4a
-        "dtype": "u8" if st.integer_exact and st.row_bytes == 128 else "f32",
-        "data": "synthetic: seeded C2 mixture (1,024 Gaussians, ints 0..255), graph from the reference build_graph settings",
+        "dtype": "u8" if st.integer_exact and st.row_bytes == base.shape[1] else "f32",
+        "data": cfg["data"],
         "config": {
-            "workload": "C2: 1M x 128 int-valued base, 10k queries per GPU, degree-32 Vamana, K=10",
+            "workload": cfg["workload"],
             "mode": args.mode, "K": K, "topk_size": chosen,
             "recall@10": sweep[-1]["recall@10"] if chosen == sweep[-1]["topk_size"] else None,
             "recall_sweep": sweep,
@@ -316,7 +376,8 @@ def run_ours(args, rank, world, local_rank):
                        if st.block_bytes else "gather"),
             "expansions_per_query": round(st.expansions / NQ_PER_GPU, 2),
             "distances_per_query": round(st.distances / NQ_PER_GPU, 2),
-            "l2": "256 MiB write before every timed step (outside the timed window); index 640 MB > L2",
+            "l2": "256 MiB write before every timed step (outside the timed window); index "
+                  f"{(base.nbytes * (st.row_bytes / (4 * base.shape[1])) + edges.nbytes) / 1e6:.0f} MB > L2",
             "parallelism": f"query-sharded dp{world}, replicated index",
         },
         "roofline": {
@@ -336,39 +397,46 @@ def run_ours(args, rank, world, local_rank):
         "clocks": clk.summary(),
     }
     if not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(base, queries, edges, chosen, entry, sample=args.cpu_sample)
+        line["cpu_baseline"] = cpu_baseline(base, queries, chosen, entry, codebook, sample=args.cpu_sample)
     return line
 
 
 # ------------------------------------------------------ reference CPU arm
 
-def _write_inputs(tmp, base, queries, edges):
+def _write_inputs(tmp, base, queries):
     from beam_search_collab_b200 import datasets as ds
     bp, qp = os.path.join(tmp, "base.fvecs"), os.path.join(tmp, "query.fvecs")
     ds.write_fvecs(bp, base)
     ds.write_fvecs(qp, queries)
-    return GRAPH_C2, bp, qp
+    return os.path.join(DATA_DIR, CFG_NAME, "graph.bin"), bp, qp
 
 
-def _ref_search(paths, topk, entry, nq, threads=None):
+def _ref_search(paths, topk, entry, nq, codebook=None, threads=None):
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
     g, b, q = paths
-    info, _ = O.run_ref_search(g, b, q, K=K, topk=topk, mode="base", threads=threads, nq=nq, entry=entry)
+    mode = "rabitq" if codebook else "base"
+    info, _ = O.run_ref_search(g, b, q, K=K, topk=topk, mode=mode, codebook=codebook, threads=threads, nq=nq,
+                               entry=entry)
     return info
 
 
-def cpu_baseline(base, queries, edges, topk, entry, sample=2000):
+def _ref_class(codebook):
+    return ("CPURabitqSearch (reference include/cpu_search_rabitq.hpp)" if codebook
+            else "CPUBaseSearch (reference include/cpu_search_base.hpp)")
+
+
+def cpu_baseline(base, queries, topk, entry, codebook=None, sample=2000):
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
     if O.ref_tool("ref_search_omp") is None:
         return {"value": None, "unit": "queries/s", "cores": 0, "kind": "reference",
                 "sample": "unavailable: oracle/_ref/ref_search_omp not built"}
     with tempfile.TemporaryDirectory() as tmp:
-        paths = _write_inputs(tmp, base, queries, edges)
-        info = _ref_search(paths, topk, entry, sample)
+        paths = _write_inputs(tmp, base, queries)
+        info = _ref_search(paths, topk, entry, min(sample, len(queries)), codebook)
     return {"value": round(info["qps"], 1), "unit": "queries/s", "cores": info["threads"], "kind": "reference",
-            "sample": f"first {info['nq']} of the 10k queries, CPUBaseSearch (reference include/cpu_search_base.hpp) "
+            "sample": f"first {info['nq']} of the {len(queries)} queries, {_ref_class(codebook)} "
                       f"under OpenMP on all host threads, topk_size {topk}, K {K}"}
 
 
@@ -379,15 +447,20 @@ def run_reference(args, rank, world):
     import oracle as O
     if O.ref_tool("ref_search_omp") is None:
         return {"impl": "reference", "unavailable": "oracle/_ref/ref_search_omp was not built from the reference tree"}
-    base, queries_all = c2_data(NQ_PER_GPU)
-    edges = load_graph()
-    topk = args.topk or 32
-    entry = O.entry_point(base)
+    cfg = CONFIGS[CFG_NAME]
+    base, queries_all, _, codebook = config_data(CFG_NAME, NQ_PER_GPU)
+    topk = args.topk or cfg.get("operating_topk") or cfg["sweep"][0]
+    entry = None
+    if codebook:   # the codebook's stored entry, as cpu_cli's rabitq path uses
+        entry = int(np.fromfile(codebook, dtype=np.uint32, count=1)[0])
+    if entry is None or entry == 0xFFFFFFFF:
+        entry = O.entry_point(base)
+    sample = min(args.ref_sample, NQ_PER_GPU)
     with tempfile.TemporaryDirectory() as tmp:
-        paths = _write_inputs(tmp, base, queries_all, edges)
+        paths = _write_inputs(tmp, base, queries_all)
         for _ in range(args.warmup):
-            _ref_search(paths, topk, entry, args.ref_sample)
-        infos = [_ref_search(paths, topk, entry, args.ref_sample) for _ in range(args.steps)]
+            _ref_search(paths, topk, entry, sample, codebook)
+        infos = [_ref_search(paths, topk, entry, sample, codebook) for _ in range(args.steps)]
     secs = sum(i["seconds"] for i in infos)
     nq = sum(i["nq"] for i in infos)
     value = nq / secs
@@ -405,24 +478,24 @@ def run_reference(args, rank, world):
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": "f32",
-        "data": "synthetic: seeded C2 mixture (1,024 Gaussians, ints 0..255), graph from the reference build_graph settings",
-        "config": {"workload": "C2: 1M x 128 int-valued base, 10k queries, degree-32 Vamana, K=10",
-                   "mode": "cpu base (CPUBaseSearch)", "K": K, "topk_size": topk,
-                   "sample_per_step": args.ref_sample},
+        "data": cfg["data"],
+        "config": {"workload": cfg["workload"], "mode": f"cpu {_ref_class(codebook)}", "K": K,
+                   "topk_size": topk, "sample_per_step": sample},
         "cpu_baseline": {"value": round(value, 1), "unit": "queries/s", "cores": cores, "kind": "reference",
-                         "sample": f"{args.ref_sample} queries per step"},
+                         "sample": f"first {sample} queries per step"},
         "e2e": {"value": round(value, 1), "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 
 
 def profile_run(args):
     """Minimal launch sequence for an ncu capture of the search kernel on the
-    full C2 workload: entry-point kernels, `warmup` searches, one search."""
+    workload's full size: entry-point kernels, `warmup` searches, one search."""
     import torch
     import beam_search_collab_b200 as B
-    base, queries = c2_data(NQ_PER_GPU)
-    edges = load_graph()
+    base, queries, edges, codebook = config_data(CFG_NAME, NQ_PER_GPU)
     ix = B.Index.from_arrays(base, edges)
+    if codebook:
+        ix.load_codebook(codebook)
     ix.entry_point()
     q = torch.from_numpy(queries).cuda()
     params = B.SearchParams(mode=args.mode, K=K, topk_size=args.topk or 32)
@@ -440,7 +513,9 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--mode", default="warp4")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="c2",
+                    help="workload (the driver's bench line is c2)")
+    ap.add_argument("--mode", default=None, help="search mode (default: the workload's)")
     ap.add_argument("--topk", type=int, default=0, help="fixed topk_size (0: sweep to the recall target)")
     ap.add_argument("--cpu-sample", type=int, default=2000)
     ap.add_argument("--ref-sample", type=int, default=1000)
@@ -448,6 +523,11 @@ def main():
     ap.add_argument("--profile-run", action="store_true",
                     help="for ncu: build the index, run `--warmup` searches and one more, print nothing else")
     args = ap.parse_args()
+    global CFG_NAME, K, NQ_PER_GPU
+    CFG_NAME = args.config
+    K = CONFIGS[CFG_NAME]["K"]
+    NQ_PER_GPU = CONFIGS[CFG_NAME]["nq"]
+    args.mode = args.mode or CONFIGS[CFG_NAME]["mode"]
     if args.profile_run:
         profile_run(args)
         return None, 0
