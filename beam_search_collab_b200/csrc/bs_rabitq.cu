@@ -148,6 +148,11 @@ __global__ void __launch_bounds__(256) k_search_rabitq(const SearchParams p) {
             }
             uint32_t c[RY];
             float tx[RY], fdq[RY], fvq[RY];
+            // codes of up to 128 padded dimensions ride along with the
+            // adjacency row (one round trip per expansion); wider codes are
+            // read after the visited test
+            uint4 code4[RY];
+            const bool code_early = wpp <= 4u;
             const uint32_t* row = p.adj + static_cast<size_t>(cur) * deg;
             const float* fac = p.factors + static_cast<size_t>(cur) * 3u * deg;
 #pragma unroll
@@ -158,6 +163,14 @@ __global__ void __launch_bounds__(256) k_search_rabitq(const SearchParams p) {
                 tx[r] = in ? __ldg(fac + pos) : FLT_MAX;
                 fdq[r] = in ? __ldg(fac + deg + pos) : 0.0f;
                 fvq[r] = in ? __ldg(fac + 2 * deg + pos) : 0.0f;
+                code4[r] = make_uint4(0u, 0u, 0u, 0u);
+                if (in && code_early) {
+                    const uint32_t* code = p.codes + (static_cast<size_t>(cur) * deg + pos) * wpp;
+                    code4[r].x = ldg_u32(code);
+                    if (wpp > 1u) code4[r].y = ldg_u32(code + 1);
+                    if (wpp > 2u) code4[r].z = ldg_u32(code + 2);
+                    if (wpp > 3u) code4[r].w = ldg_u32(code + 3);
+                }
             }
 
             // exact distance of the expanded node (include/cpu_search_rabitq.hpp:130)
@@ -204,7 +217,11 @@ __global__ void __launch_bounds__(256) k_search_rabitq(const SearchParams p) {
                     const uint32_t* code = p.codes + (static_cast<size_t>(cur) * deg + pos) * wpp;
                     uint32_t raw = 0;
                     for (uint32_t wd = 0; wd < wpp; ++wd) {
-                        const uint32_t cw = ldg_u32(code + wd);
+                        uint32_t cw;
+                        if (code_early)
+                            cw = wd == 0 ? code4[r].x : wd == 1 ? code4[r].y : wd == 2 ? code4[r].z : code4[r].w;
+                        else
+                            cw = ldg_u32(code + wd);
 #pragma unroll
                         for (int b = 0; b < kPlanes; ++b)
                             raw += static_cast<uint32_t>(__popc(planes[b * wpp + wd] & cw)) << b;
