@@ -106,6 +106,7 @@ struct SearchParams {
     // staging
     uint32_t stage_rows;        // rows staged per round in kSeq mode
     uint32_t stage_pitch;       // floats between staged rows (odd multiple of 4)
+    uint32_t stage_ring;        // kSeq wide rows: 1 = stream row chunks through a ring (bs_score.cuh)
     // per-warp shared-memory carve-up (bytes)
     uint32_t smem_per_warp;
     uint32_t off_q8;            // kU8: the query as packed u8 (row_bytes)

@@ -53,6 +53,66 @@ __device__ __forceinline__ void score_rows_seq(const SearchParams& p, uint32_t m
     }
 }
 
+// Wide rows (the 960-d C4 rows are 3.84 KB): the same sequential order, with
+// the rows streamed through a ring of kRingStages chunks of kRingCh
+// dimensions of up to 32 rows -- every lane folds its own row while the next
+// chunks are in flight -- so a warp holds kRingStages * 32 * kRingPitch
+// floats of shared memory instead of whole rows.  Each lane keeps its running
+// sum in a register across chunks and adds the elements d = 0..row_stride-1
+// in order with separately rounded operations: the reference's bits (the zero
+// pad of the stored rows and of the query adds +0).
+constexpr uint32_t kRingCh = 32;       // dimensions per chunk
+constexpr uint32_t kRingStages = 4;    // chunks in the ring (3 in flight while one is folded)
+constexpr uint32_t kRingPitch = 36;    // floats per staged row chunk: 9 16-byte units, odd
+constexpr uint32_t kRingFloats = kRingStages * 32u * kRingPitch;
+
+__device__ __forceinline__ void score_rows_seq_ring(const SearchParams& p, uint32_t m, const uint32_t* cids,
+                                                    float* cdist, const float* qsm, float* ring,
+                                                    unsigned lane) {
+    const uint32_t nch = (p.row_stride + kRingCh - 1) / kRingCh;
+    const uint32_t part = lane & 7u;     // 16-byte piece of a row chunk this lane copies
+    for (uint32_t g0 = 0; g0 < m; g0 += 32) {
+        const uint32_t rows = min(32u, m - g0);
+        // one commit group per chunk (empty past the last one), so that
+        // wait_group kRingStages-1 always means "chunk c has landed"
+        auto issue = [&](uint32_t c) {
+            if (c < nch) {
+                const uint32_t d = c * kRingCh + part * 4u;
+                float* st = ring + (c % kRingStages) * 32u * kRingPitch + part * 4u;
+                if (d < p.row_stride)
+                    for (uint32_t r = lane >> 3; r < rows; r += 4)
+                        cp_async16(st + r * kRingPitch, p.vecs + static_cast<size_t>(cids[g0 + r]) * p.row_stride + d);
+            }
+            asm volatile("cp.async.commit_group;\n" ::: "memory");
+        };
+        for (uint32_t c = 0; c + 1 < kRingStages; ++c) issue(c);
+        float acc = 0.0f;
+        for (uint32_t c = 0; c < nch; ++c) {
+            issue(c + kRingStages - 1);
+            asm volatile("cp.async.wait_group %0;\n" ::"n"(kRingStages - 1) : "memory");
+            __syncwarp();
+            if (lane < rows) {
+                const float* x = ring + (c % kRingStages) * 32u * kRingPitch + lane * kRingPitch;
+                const uint32_t d0 = c * kRingCh;
+                const uint32_t n4 = min(kRingCh, p.row_stride - d0) / 4u;
+                for (uint32_t j = 0; j < n4; ++j) {
+                    const float4 v = *reinterpret_cast<const float4*>(x + 4u * j);
+                    const float4 q = *reinterpret_cast<const float4*>(qsm + d0 + 4u * j);
+                    float t;
+                    t = __fsub_rn(q.x, v.x); acc = __fadd_rn(acc, __fmul_rn(t, t));
+                    t = __fsub_rn(q.y, v.y); acc = __fadd_rn(acc, __fmul_rn(t, t));
+                    t = __fsub_rn(q.z, v.z); acc = __fadd_rn(acc, __fmul_rn(t, t));
+                    t = __fsub_rn(q.w, v.w); acc = __fadd_rn(acc, __fmul_rn(t, t));
+                }
+            }
+            __syncwarp();   // this stage is refilled by the next iteration's issue
+        }
+        if (lane < rows) cdist[g0 + lane] = acc;
+        asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+        __syncwarp();
+    }
+}
+
 // Same order without staging: lane i reads row i straight from global
 // memory.  Used by the integer-exact kernels for a query that does not meet
 // the integer condition (those kernels carry no staging area).
@@ -246,7 +306,8 @@ __device__ __forceinline__ void score_rows(const SearchParams& p, uint32_t m, co
                                            float* cdist, const float* qsm, const uint32_t* q8,
                                            float* stage, unsigned lane, bool team_ok) {
     if (DM == kSeq) {
-        score_rows_seq(p, m, cids, cdist, qsm, stage, lane);
+        if (p.stage_ring) score_rows_seq_ring(p, m, cids, cdist, qsm, stage, lane);
+        else score_rows_seq(p, m, cids, cdist, qsm, stage, lane);
     } else if (DM == kTeam) {
         if (team_ok) score_rows_team(p, m, cids, cdist, qsm, lane);
         else score_rows_seq_direct(p, m, cids, cdist, qsm, lane);

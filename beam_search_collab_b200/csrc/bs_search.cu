@@ -352,7 +352,17 @@ cudaError_t plan_search(SearchParams& p, LaunchShape& shape, size_t max_smem_opt
         if (rows > cand) rows = cand;
         if (rows < 1u) rows = 1u;
         p.stage_rows = rows;
-        off = align16(off + rows * row_bytes);
+        p.stage_ring = 0;
+        if (p.codes == nullptr && row_bytes > 1024u) {
+            // wide rows (C4: 3.84 KB): whole-row staging held 12 rows per warp
+            // (one 4-warp block per SM, 12 of 32 lanes folding); a ring of row
+            // chunks keeps all 32 lanes folding in 18 KB per warp
+            p.stage_ring = 1;
+            p.stage_rows = 0;
+            off = align16(off + dev::kRingFloats * 4u);
+        } else {
+            off = align16(off + rows * row_bytes);
+        }
     } else {
         p.stage_rows = 0;
     }

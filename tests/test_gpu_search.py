@@ -237,6 +237,32 @@ def test_large_host_batch_matches_device_batch_and_golden_rows(indexes, name, mo
         assert (ids_h[:nq0] == exp).all()
 
 
+@pytest.mark.parametrize("deg", [24, 48])
+def test_wide_rows_stream_through_the_chunk_ring_and_stay_exact(monkeypatch, deg):
+    """Float rows wider than 1 KB in the gather layout are folded chunk by
+    chunk through a shared-memory ring; every distance must still equal the
+    reference's sequential order bit for bit (dim 300: a partial last chunk;
+    degree 48: two groups of rows per expansion)."""
+    rng = np.random.default_rng(5 + deg)
+    n, dim = 4000, 300
+    base = (rng.standard_normal((n, dim)) * 2).astype(np.float32)
+    q = (rng.standard_normal((40, dim)) * 2).astype(np.float32)
+    edges = rng.integers(0, n, size=(n, deg), dtype=np.uint32)
+    monkeypatch.setenv("BSEARCH_LAYOUT", "gather")
+    ix = B.Index.from_arrays(base, edges)
+    monkeypatch.delenv("BSEARCH_LAYOUT")
+    try:
+        entry = O.entry_point(base)
+        for mode, K, topk in (("warp4", 10, 64), ("base", 32, 128)):
+            ids, d, st = ix.search(q, mode=mode, K=K, topk_size=topk)
+            ref = O.search(base, edges, q, K=K, topk_size=topk, entry=entry)
+            assert np.array_equal(ids, ref.ids)
+            assert np.array_equal(d.view(np.uint32), ref.dists.view(np.uint32))
+            assert st.distances == ref.stats.distances or st.distances > ref.stats.distances
+    finally:
+        ix.close()
+
+
 def test_k_larger_than_beam_pads_with_no_node(indexes):
     g, ix = indexes["f48"]
     ids, dists, _ = ix.search(g.queries[:8], mode="warp1", K=80, topk_size=32)
