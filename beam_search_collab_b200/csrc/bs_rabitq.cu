@@ -35,7 +35,7 @@ namespace {
 constexpr int kPlanes = 7;   // quantised query values are 1..64
 
 template <int RX, int RY, int DM>
-__global__ void __launch_bounds__(256) k_search_rabitq(const SearchParams p) {
+__global__ void __launch_bounds__(128, (RX <= 8 ? 5 : 2)) k_search_rabitq(const SearchParams p) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const unsigned lane = threadIdx.x & 31u;
     unsigned char* ws = smem_raw + static_cast<size_t>(threadIdx.x >> 5) * p.smem_per_warp;
