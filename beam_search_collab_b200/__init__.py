@@ -68,7 +68,7 @@ class Stats(ctypes.Structure):
 
 # Every symbol include/bsearch.h declares (checked by the CPU test suite).
 EXPORTS = ("bs_search_params_default", "bs_index_create", "bs_index_load", "bs_index_attach_rabitq",
-           "bs_index_load_codebook", "bs_index_info", "bs_index_entry_point", "bs_index_rabitq_entry",
+           "bs_index_load_codebook", "bs_index_build_codebook", "bs_index_info", "bs_index_entry_point", "bs_index_rabitq_entry",
            "bs_index_destroy", "bs_search", "bs_search_no_alloc", "bs_merge_shards", "bs_device_alloc",
            "bs_device_free",
            "bs_copy_to_device",
@@ -92,6 +92,7 @@ def lib() -> ctypes.CDLL:
     L.bs_index_load.argtypes = [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_int, ctypes.POINTER(vp)]
     L.bs_index_attach_rabitq.argtypes = [vp, ctypes.POINTER(_RabitqDesc)]
     L.bs_index_load_codebook.argtypes = [vp, ctypes.c_char_p]
+    L.bs_index_build_codebook.argtypes = [vp, ctypes.c_uint32, ctypes.c_char_p, _u32p]
     L.bs_index_info.argtypes = [vp, ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_int32),
                                 ctypes.POINTER(ctypes.c_int32)]
     L.bs_index_entry_point.argtypes = [vp, _u32p]
@@ -112,6 +113,7 @@ def lib() -> ctypes.CDLL:
     L.bs_device_fill.argtypes = [vp, vp, ctypes.c_int, ctypes.c_size_t]
     L.bs_synchronize.argtypes = [vp, vp]
     for f in ("bs_index_create", "bs_index_load", "bs_index_attach_rabitq", "bs_index_load_codebook",
+              "bs_index_build_codebook",
               "bs_index_info", "bs_index_entry_point", "bs_index_rabitq_entry", "bs_search",
               "bs_device_alloc", "bs_device_free", "bs_copy_to_device", "bs_copy_to_host",
               "bs_device_fill", "bs_synchronize"):
@@ -194,6 +196,16 @@ class Index:
 
     def load_codebook(self, path: str) -> None:
         _check(lib().bs_index_load_codebook(self._h, path.encode()))
+
+    def build_codebook(self, seed: int = 12345, out_path: str | None = None) -> int:
+        """Builds the RaBitQ codebook of this index on the GPU (the reference
+        build_rabitq rule and arithmetic, src/build_rabitq.cpp:120-285),
+        attaches it, optionally writes it as codebook.bin; returns the medoid
+        entry point."""
+        e = ctypes.c_uint32()
+        _check(lib().bs_index_build_codebook(self._h, seed, out_path.encode() if out_path else None,
+                                             ctypes.byref(e)))
+        return e.value
 
     def close(self) -> None:
         if self._h and self._h.value:

@@ -18,6 +18,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <random>
 #include <string>
 #include <thread>
 #include <vector>
@@ -141,38 +142,42 @@ bool parse_mode(const char* m, ModeInfo& mi) {
     return false;
 }
 
-// Range of the values and whether every value is an integer (multi-threaded
-// scan of the host array at index creation).
-void scan_values(const float* v, uint64_t count, bool& all_int, float& min_val, float& max_val) {
+// Range of the values, whether every value is an integer and whether any is
+// -0.0 (multi-threaded scan of the host array at index creation).
+void scan_values(const float* v, uint64_t count, bool& all_int, bool& neg_zero, float& min_val, float& max_val) {
     unsigned nt = std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
     if (count < (1u << 20)) nt = 1;
-    std::vector<char> ints(nt, 1);
+    std::vector<char> ints(nt, 1), nzs(nt, 0);
     std::vector<float> mins(nt, 0.0f), maxes(nt, 0.0f);
     std::vector<std::thread> th;
     const uint64_t per = (count + nt - 1) / nt;
     for (unsigned t = 0; t < nt; ++t) {
         th.emplace_back([&, t] {
             const uint64_t lo = per * t, hi = std::min(count, lo + per);
-            bool ok = true;
+            bool ok = true, nz = false;
             float mn = lo < hi ? v[lo] : 0.0f, mx = mn;
             for (uint64_t i = lo; i < hi; ++i) {
                 const float x = v[i];
                 ok = ok && (x == std::nearbyint(x));   // false for NaN and inf
+                nz = nz || (x == 0.0f && std::signbit(x));
                 mn = x < mn ? x : mn;
                 mx = x > mx ? x : mx;
             }
             ints[t] = ok;
+            nzs[t] = nz;
             mins[t] = mn;
             maxes[t] = mx;
         });
     }
     for (auto& t : th) t.join();
     all_int = true;
+    neg_zero = false;
     min_val = mins[0];
     max_val = maxes[0];
     for (unsigned t = 0; t < nt; ++t) {
         if (per * t >= count) continue;
         all_int = all_int && ints[t];
+        neg_zero = neg_zero || nzs[t];
         min_val = std::min(min_val, mins[t]);
         max_val = std::max(max_val, maxes[t]);
     }
@@ -413,10 +418,14 @@ BS_API bs_status bs_index_create(const bs_graph_desc* desc, int device, bs_index
     ix->num_sms = prop.multiProcessorCount;
     ix->smem_optin = prop.sharedMemPerBlockOptin;
 
-    scan_values(desc->vectors, static_cast<uint64_t>(ix->n) * ix->dim, ix->int_exact, ix->min_val, ix->max_val);
+    bool neg_zero = false;
+    scan_values(desc->vectors, static_cast<uint64_t>(ix->n) * ix->dim, ix->int_exact, neg_zero, ix->min_val,
+                ix->max_val);
     // Exact byte copy when every value is an integer in [0,255] (SIFT-like
     // data): a quarter of the HBM bytes per gathered row, integer distances.
-    ix->u8 = ix->int_exact && ix->min_val >= 0.0f && ix->max_val <= 255.0f && !storage_f32_forced();
+    // byte rows only when the copy is exact bit for bit (-0.0 would come back
+    // as +0.0 in the rows a written codebook carries)
+    ix->u8 = ix->int_exact && !neg_zero && ix->min_val >= 0.0f && ix->max_val <= 255.0f && !storage_f32_forced();
     ix->row_bytes = (static_cast<uint32_t>(desc->dim) + 15u) & ~15u;
 
     const size_t ebytes = static_cast<size_t>(ix->n) * ix->degree * sizeof(uint32_t);
@@ -517,6 +526,123 @@ BS_API bs_status bs_index_load_codebook(bs_index* ix, const char* path) {
     if (!bsb::io::read_codebook(path, ix->n, ix->dim, ix->degree, cb, err)) return fail(BS_ERR_IO, "%s", err.c_str());
     bs_rabitq_desc d{cb.entry, cb.padded_dim, cb.codes.data(), cb.factors.data(), cb.signs.data()};
     return bs_index_attach_rabitq(ix, &d);
+}
+
+BS_API bs_status bs_index_build_codebook(bs_index* ix, uint32_t seed, const char* out_path, uint32_t* entry_out) {
+    if (!ix) return fail(BS_ERR_INVALID_ARGUMENT, "index is NULL");
+    const int32_t pdim = bsb::io::padded_dim_of(ix->dim);
+    if (pdim < 32) return fail(BS_ERR_UNSUPPORTED, "RaBitQ needs dim > 16 (padded_dim >= 32)");
+    if (ix->n > 0xffffffffull) return fail(BS_ERR_UNSUPPORTED, "more than 2^32 rows");
+    // sign table: the reference's generator and distribution
+    // (src/build_rabitq.cpp:138-146), from the same standard library
+    std::vector<float> signs(static_cast<size_t>(pdim));
+    {
+        std::mt19937_64 gen(seed);
+        std::uniform_int_distribution<int> coin(0, 1);
+        const float scale = 1.0f / std::sqrt(static_cast<float>(pdim));
+        for (int32_t i = 0; i < pdim; ++i) signs[static_cast<size_t>(i)] = static_cast<float>(2 * coin(gen) - 1) * scale;
+    }
+    DeviceGuard g(ix->device);
+    if (!g.ok) return fail(BS_ERR_CUDA, "cannot select device %d", ix->device);
+    const size_t wpp = static_cast<size_t>(pdim) / 32;
+    const size_t deg = static_cast<size_t>(ix->degree);
+    const size_t cbytes = static_cast<size_t>(ix->n) * deg * wpp * 4;
+    const size_t fbytes = static_cast<size_t>(ix->n) * 3 * deg * 4;
+    uint32_t* d_codes = nullptr;
+    float* d_factors = nullptr;
+    float* d_signs = nullptr;
+    unsigned char* d_scratch = nullptr;
+    uint32_t* d_stage = nullptr;
+    std::FILE* f = nullptr;
+    auto cleanup = [&]() {
+        cudaFree(d_codes);
+        cudaFree(d_factors);
+        cudaFree(d_signs);
+        cudaFree(d_scratch);
+        cudaFree(d_stage);
+        if (f) std::fclose(f);
+    };
+    cudaError_t e;
+    if ((e = cudaMalloc(&d_codes, cbytes ? cbytes : 4)) != cudaSuccess ||
+        (e = cudaMalloc(&d_factors, fbytes ? fbytes : 4)) != cudaSuccess ||
+        (e = cudaMalloc(&d_signs, static_cast<size_t>(pdim) * 4)) != cudaSuccess ||
+        (e = cudaMalloc(&d_scratch, bsb::medoid_scratch_bytes(static_cast<uint32_t>(ix->dim)) + 16)) != cudaSuccess) {
+        cleanup();
+        return cuda_fail(e, "codebook buffers");
+    }
+    if ((e = cudaMemcpy(d_signs, signs.data(), static_cast<size_t>(pdim) * 4, cudaMemcpyHostToDevice)) != cudaSuccess) {
+        cleanup();
+        return cuda_fail(e, "sign table upload");
+    }
+    bsb::CodebookArgs a{};
+    a.vecs = ix->u8 ? nullptr : ix->d_vecs;
+    a.vecs8 = ix->u8 ? ix->d_vecs8 : nullptr;
+    a.row_stride = ix->u8 ? ix->row_bytes : ix->row_stride;
+    a.adj = ix->d_adj;
+    a.n = ix->n;
+    a.dim = static_cast<uint32_t>(ix->dim);
+    a.degree = static_cast<uint32_t>(ix->degree);
+    a.pdim = static_cast<uint32_t>(pdim);
+    a.signs = d_signs;
+    a.codes = d_codes;
+    a.factors = d_factors;
+    uint32_t* d_entry = reinterpret_cast<uint32_t*>(d_scratch + bsb::medoid_scratch_bytes(a.dim));
+    uint32_t entry = BS_NO_NODE;
+    if ((e = bsb::compute_medoid(a, d_entry, d_scratch, 0)) != cudaSuccess ||
+        (e = bsb::quantize_edges(a, ix->smem_optin, ix->num_sms, 0)) != cudaSuccess ||
+        (e = cudaMemcpy(&entry, d_entry, 4, cudaMemcpyDeviceToHost)) != cudaSuccess) {
+        cleanup();
+        return cuda_fail(e, "codebook build");
+    }
+    if (out_path) {
+        // codebook.bin (src/build_rabitq.cpp:268-285): u32 entry, n rows, signs
+        f = std::fopen(out_path, "wb");
+        if (!f) {
+            cleanup();
+            return fail(BS_ERR_IO, "Cannot open output file: %s", out_path);
+        }
+        const uint64_t row_slots = static_cast<uint64_t>(ix->dim) + wpp * deg + 4 * deg;
+        const uint64_t chunk = std::max<uint64_t>(1, (256ull << 20) / (row_slots * 4));
+        const uint64_t rows = std::min<uint64_t>(chunk, ix->n);
+        std::vector<uint32_t> host(static_cast<size_t>(rows * row_slots));
+        bool ok = std::fwrite(&entry, 4, 1, f) == 1;
+        if (ok && rows && (e = cudaMalloc(&d_stage, rows * row_slots * 4)) != cudaSuccess) {
+            cleanup();
+            return cuda_fail(e, "codebook staging");
+        }
+        for (uint64_t r0 = 0; ok && r0 < ix->n; r0 += rows) {
+            const uint64_t cnt = std::min<uint64_t>(rows, ix->n - r0);
+            if ((e = bsb::pack_codebook_rows(a, r0, cnt, d_stage, ix->num_sms, 0)) != cudaSuccess ||
+                (e = cudaMemcpy(host.data(), d_stage, cnt * row_slots * 4, cudaMemcpyDeviceToHost)) != cudaSuccess) {
+                cleanup();
+                return cuda_fail(e, "codebook rows");
+            }
+            ok = std::fwrite(host.data(), 4, cnt * row_slots, f) == cnt * row_slots;
+        }
+        ok = ok && std::fwrite(signs.data(), 4, static_cast<size_t>(pdim), f) == static_cast<size_t>(pdim);
+        ok = (std::fclose(f) == 0) && ok;
+        f = nullptr;
+        if (!ok) {
+            cleanup();
+            return fail(BS_ERR_IO, "Cannot write codebook: %s", out_path);
+        }
+    }
+    cudaFree(d_stage);
+    d_stage = nullptr;
+    cudaFree(d_scratch);
+    d_scratch = nullptr;
+    // attach (replacing any previous codebook)
+    cudaFree(ix->d_codes);
+    cudaFree(ix->d_factors);
+    cudaFree(ix->d_signs);
+    ix->d_codes = d_codes;
+    ix->d_factors = d_factors;
+    ix->d_signs = d_signs;
+    ix->pdim = pdim;
+    ix->rq_entry = entry;
+    ix->has_rabitq = true;
+    if (entry_out) *entry_out = entry;
+    return BS_OK;
 }
 
 BS_API bs_status bs_index_info(const bs_index* ix, uint64_t* n, int32_t* dim, int32_t* degree) {

@@ -165,6 +165,28 @@ struct MergeArgs {
 };
 cudaError_t launch_merge_shards(const MergeArgs& a, int num_sms, cudaStream_t stream);
 
+// RaBitQ codebook builder (bs_codebook.cu).
+constexpr uint32_t kMedoidBlocks = 1184;
+struct CodebookArgs {
+    const float* vecs;           // [n][row_stride] f32, or null
+    const uint8_t* vecs8;        // [n][row_stride] u8 (exact byte copy), or null
+    uint32_t row_stride;         // elements per stored row
+    const uint32_t* adj;         // [n][degree]
+    uint64_t n;
+    uint32_t dim, degree, pdim;  // pdim: next power of two >= dim, >= 32
+    const float* signs;          // [pdim] (device)
+    uint32_t* codes;             // [n][degree][pdim/32]
+    float* factors;              // [n][3][degree]
+    uint32_t batch_rows;         // set by the launcher
+    uint32_t smem_floats_per_warp;
+};
+size_t medoid_scratch_bytes(uint32_t dim);
+cudaError_t compute_medoid(const CodebookArgs& a, uint32_t* d_result, void* d_scratch, cudaStream_t stream);
+cudaError_t quantize_edges(const CodebookArgs& a, size_t smem_optin, int num_sms, cudaStream_t stream);
+// rows [first, first + count) in the codebook.bin row layout into out (device)
+cudaError_t pack_codebook_rows(const CodebookArgs& a, uint64_t first, uint64_t count, uint32_t* out, int num_sms,
+                               cudaStream_t stream);
+
 // Entry point (bs_entry.cu): centroid-nearest row, reference arithmetic, over
 // f32 rows (vecs) or exact u8 rows (vecs8, row stride in bytes).
 cudaError_t compute_entry_point(const float* vecs, uint64_t n, uint32_t dim, uint32_t row_stride,

@@ -111,6 +111,17 @@ BS_API bs_status bs_index_attach_rabitq(bs_index* index, const bs_rabitq_desc* d
 /* Replaces load_rabitq_codebook (include/rabitq.hpp:49-97) + GPURabitq. */
 BS_API bs_status bs_index_load_codebook(bs_index* index, const char* codebook_path);
 
+/* Replaces the reference codebook builder (src/build_rabitq.cpp:120-285),
+ * on the GPU over the index's own rows and graph: sign table from
+ * std::mt19937_64(seed) as build_rabitq -seed, medoid entry point, per-edge
+ * codes and factors with the same arithmetic (bit-identical).  The result is
+ * attached to the index as bs_index_load_codebook would attach it; when
+ * out_path is non-NULL it is also written there in the codebook.bin format,
+ * byte-identical to the reference tool's file.  entry_out (nullable)
+ * receives the medoid.  Needs padded_dim >= 32 (dim > 16). */
+BS_API bs_status bs_index_build_codebook(bs_index* index, uint32_t seed, const char* out_path,
+                                         uint32_t* entry_out);
+
 BS_API bs_status bs_index_info(const bs_index* index, uint64_t* num_nodes, int32_t* dim,
                                int32_t* degree);
 
