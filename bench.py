@@ -8,7 +8,7 @@ recall@10 against the exact top-10 is >= 0.95; a "step" is one search of all
 of a GPU's queries at that point.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--config c2|c3|c4]
+                    [--config c2|c3|c4] [--measure search|codebook]
 
 --config selects another BASELINE.json workload for measurement (default and
 the driver's line: c2): c3 = RaBitQ search (1M x 96 unit vectors, degree 64,
@@ -25,6 +25,10 @@ Arms
   reference  : the reference's own CPU search (CPUBaseSearch through
                oracle/_ref/ref_search_omp, all host cores), same data, K and
                topk; each step a bounded sample of the queries.
+
+--measure codebook times the GPU RaBitQ codebook builder on the workload's
+base and graph instead (one JSON line, edges/s; the reference build_rabitq on
+all host threads as the CPU baseline, and the two codebook files compared).
 
 Multi-GPU (torchrun, one rank per GPU): query sharding over a replicated
 index, no collective on the data path; every rank searches its own 10,000
@@ -93,7 +97,17 @@ def config_data(name: str, nq_total: int):
         raise SystemExit(f"missing {graph}: build it with the reference build_graph over the {name} base")
     cb = os.path.join(DATA_DIR, name, "codebook.bin") if cfg["codebook"] else None
     if cb and not os.path.exists(cb):
-        raise SystemExit(f"missing {cb}: build it with the reference build_rabitq (-seed 12345)")
+        # too large to ship (2.4 GB for C3): the reference build_rabitq makes it here
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as O
+        tool = O.ref_tool("build_rabitq")
+        if tool is None:
+            raise SystemExit(f"missing {cb}: build it with the reference build_rabitq (-seed 12345)")
+        with tempfile.TemporaryDirectory() as tmp:
+            bp = os.path.join(tmp, "base.fvecs")
+            ds.write_fvecs(bp, s.base)
+            subprocess.run([tool, "-base", bp, "-graph", graph, "-out", cb, "-seed", "12345"], check=True,
+                           stdout=subprocess.DEVNULL)
     return s.base, s.queries, ds.read_graph(graph), cb
 
 
@@ -492,6 +506,16 @@ def profile_run(args):
     workload's full size: entry-point kernels, `warmup` searches, one search."""
     import torch
     import beam_search_collab_b200 as B
+    if args.measure == "codebook":
+        # the builder's kernels: `warmup` builds and one more
+        from beam_search_collab_b200 import datasets as ds
+        s = getattr(ds, CONFIGS[CFG_NAME]["gen"])(nq=1)
+        ix = B.Index.from_arrays(s.base, ds.read_graph(os.path.join(DATA_DIR, CFG_NAME, "graph.bin")))
+        for _ in range(args.warmup + 1):
+            ix.build_codebook(12345)
+        torch.cuda.synchronize()
+        log("profile run done")
+        return
     base, queries, edges, codebook = config_data(CFG_NAME, NQ_PER_GPU)
     ix = B.Index.from_arrays(base, edges)
     if codebook:
@@ -503,6 +527,77 @@ def profile_run(args):
         ix.search(q, params)
     torch.cuda.synchronize()
     log("profile run done")
+
+
+def measure_codebook(args):
+    """--measure codebook: the GPU codebook builder (bs_index_build_codebook)
+    over the workload's base and graph.  value = edges quantized per second,
+    device time of the whole call (medoid, sign table upload, quantization,
+    buffers) with CUDA events, L2 flushed before each step; e2e = the drop-in
+    CLI bin/build_rabitq end to end (read files, upload, build, write
+    codebook.bin), wall clock; cpu_baseline = the reference build_rabitq on
+    the same files with all host threads, wall clock; `identical` = the two
+    files compared byte for byte."""
+    import filecmp
+    import torch
+    import beam_search_collab_b200 as B
+    from beam_search_collab_b200 import datasets as ds
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    s = getattr(ds, CONFIGS[CFG_NAME]["gen"])(nq=1)
+    graph = os.path.join(DATA_DIR, CFG_NAME, "graph.bin")
+    ix = B.Index.from_arrays(s.base, ds.read_graph(graph))
+    n, dim, deg = ix.info()
+    for _ in range(args.warmup):
+        ix.build_codebook(12345)
+    torch.cuda.synchronize()
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+    times = []
+    for _ in range(args.steps):
+        flush.fill_(1)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        ix.build_codebook(12345)
+        b.record()
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b))
+    ms = statistics.median(times)
+    entry = ix.rabitq_entry()
+    ix.close()
+    edges = n * deg
+    with tempfile.TemporaryDirectory() as tmp:
+        bp = os.path.join(tmp, "base.fvecs")
+        ds.write_fvecs(bp, s.base)
+        ours, ref = os.path.join(tmp, "ours.bin"), os.path.join(tmp, "ref.bin")
+        t = time.perf_counter()
+        subprocess.run([os.path.join(ROOT, "beam_search_collab_b200", "bin", "build_rabitq"), "-base", bp, "-graph",
+                        graph, "-out", ours, "-seed", "12345"], check=True, stdout=subprocess.DEVNULL)
+        e2e_s = time.perf_counter() - t
+        tool = O.ref_tool("build_rabitq")
+        ref_s, identical = None, None
+        if tool is not None:
+            t = time.perf_counter()
+            subprocess.run([tool, "-base", bp, "-graph", graph, "-out", ref, "-seed", "12345"], check=True,
+                           stdout=subprocess.DEVNULL)
+            ref_s = time.perf_counter() - t
+            identical = filecmp.cmp(ours, ref, shallow=False)
+        file_bytes = os.path.getsize(ours)
+    return {
+        "metric": "codebook_build_edges_per_s", "value": round(edges / (ms / 1e3)), "unit": "edges/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+        "higher_is_better": True, "scaling": "none", "vs_baseline": None, "dtype": "f32",
+        "data": CONFIGS[CFG_NAME]["data"],
+        "config": {"workload": f"RaBitQ codebook of {CFG_NAME}: {n} nodes x {deg} edges, dim {dim}, seed 12345",
+                   "l2": "flushed (256 MiB write) before every timed step", "medoid_entry": entry},
+        "e2e": {"value": round(edges / e2e_s), "unit": "edges/s", "seconds": round(e2e_s, 3),
+                "file_bytes": file_bytes, "h2d_bytes_per_step": None, "d2h_bytes_per_step": file_bytes},
+        "cpu_baseline": {"value": round(edges / ref_s) if ref_s else None, "unit": "edges/s",
+                         "seconds": round(ref_s, 3) if ref_s else None, "cores": os.cpu_count(),
+                         "kind": "reference",
+                         "sample": "the whole build, reference build_rabitq (oracle/_ref) under OpenMP on all "
+                                   "host threads, wall clock incl. its file reads and codebook write"},
+        "identical": identical,
+    }
 
 
 # -------------------------------------------------------------------- main
@@ -520,6 +615,8 @@ def main():
     ap.add_argument("--cpu-sample", type=int, default=2000)
     ap.add_argument("--ref-sample", type=int, default=1000)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--measure", choices=("search", "codebook"), default="search",
+                    help="codebook: time the GPU codebook builder instead of the search")
     ap.add_argument("--profile-run", action="store_true",
                     help="for ncu: build the index, run `--warmup` searches and one more, print nothing else")
     args = ap.parse_args()
@@ -532,6 +629,8 @@ def main():
         profile_run(args)
         return None, 0
     args.warmup = max(args.warmup, 3)
+    if args.measure == "codebook":
+        return measure_codebook(args), 0
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
