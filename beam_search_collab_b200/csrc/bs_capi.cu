@@ -49,6 +49,7 @@ struct bs_index {
     unsigned char* d_nb = nullptr;
     uint32_t nb_stride = 0, nb_adj_bytes = 0, nb_pitch = 0;
     bool int_exact = false;      // every base value an integer
+    std::vector<uint64_t> neg_zeros;  // byte rows: flat positions of -0.0 values (ascending)
     float min_val = 0.0f;        // range of the base values
     float max_val = 0.0f;
     // RaBitQ
@@ -144,40 +145,41 @@ bool parse_mode(const char* m, ModeInfo& mi) {
 
 // Range of the values, whether every value is an integer and whether any is
 // -0.0 (multi-threaded scan of the host array at index creation).
-void scan_values(const float* v, uint64_t count, bool& all_int, bool& neg_zero, float& min_val, float& max_val) {
+void scan_values(const float* v, uint64_t count, bool& all_int, std::vector<uint64_t>& neg_zeros, float& min_val,
+                 float& max_val) {
     unsigned nt = std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
     if (count < (1u << 20)) nt = 1;
-    std::vector<char> ints(nt, 1), nzs(nt, 0);
+    std::vector<char> ints(nt, 1);
+    std::vector<std::vector<uint64_t>> nzs(nt);
     std::vector<float> mins(nt, 0.0f), maxes(nt, 0.0f);
     std::vector<std::thread> th;
     const uint64_t per = (count + nt - 1) / nt;
     for (unsigned t = 0; t < nt; ++t) {
         th.emplace_back([&, t] {
             const uint64_t lo = per * t, hi = std::min(count, lo + per);
-            bool ok = true, nz = false;
+            bool ok = true;
             float mn = lo < hi ? v[lo] : 0.0f, mx = mn;
             for (uint64_t i = lo; i < hi; ++i) {
                 const float x = v[i];
                 ok = ok && (x == std::nearbyint(x));   // false for NaN and inf
-                nz = nz || (x == 0.0f && std::signbit(x));
+                if (x == 0.0f && std::signbit(x)) nzs[t].push_back(i);
                 mn = x < mn ? x : mn;
                 mx = x > mx ? x : mx;
             }
             ints[t] = ok;
-            nzs[t] = nz;
             mins[t] = mn;
             maxes[t] = mx;
         });
     }
     for (auto& t : th) t.join();
     all_int = true;
-    neg_zero = false;
+    neg_zeros.clear();
     min_val = mins[0];
     max_val = maxes[0];
     for (unsigned t = 0; t < nt; ++t) {
         if (per * t >= count) continue;
         all_int = all_int && ints[t];
-        neg_zero = neg_zero || nzs[t];
+        neg_zeros.insert(neg_zeros.end(), nzs[t].begin(), nzs[t].end());
         min_val = std::min(min_val, mins[t]);
         max_val = std::max(max_val, maxes[t]);
     }
@@ -418,14 +420,17 @@ BS_API bs_status bs_index_create(const bs_graph_desc* desc, int device, bs_index
     ix->num_sms = prop.multiProcessorCount;
     ix->smem_optin = prop.sharedMemPerBlockOptin;
 
-    bool neg_zero = false;
-    scan_values(desc->vectors, static_cast<uint64_t>(ix->n) * ix->dim, ix->int_exact, neg_zero, ix->min_val,
-                ix->max_val);
+    std::vector<uint64_t> neg_zeros;
+    const uint64_t nvals = static_cast<uint64_t>(ix->n) * ix->dim;
+    scan_values(desc->vectors, nvals, ix->int_exact, neg_zeros, ix->min_val, ix->max_val);
     // Exact byte copy when every value is an integer in [0,255] (SIFT-like
     // data): a quarter of the HBM bytes per gathered row, integer distances.
-    // byte rows only when the copy is exact bit for bit (-0.0 would come back
-    // as +0.0 in the rows a written codebook carries)
-    ix->u8 = ix->int_exact && !neg_zero && ix->min_val >= 0.0f && ix->max_val <= 255.0f && !storage_f32_forced();
+    // byte rows lose the sign of -0.0 (no distance depends on it, but the
+    // rows a written codebook carries must come back bit for bit): their flat
+    // positions are kept on the host, as long as they are few
+    ix->u8 = ix->int_exact && ix->min_val >= 0.0f && ix->max_val <= 255.0f && !storage_f32_forced() &&
+             neg_zeros.size() <= nvals / 64;
+    if (ix->u8) ix->neg_zeros.swap(neg_zeros);
     ix->row_bytes = (static_cast<uint32_t>(desc->dim) + 15u) & ~15u;
 
     const size_t ebytes = static_cast<size_t>(ix->n) * ix->degree * sizeof(uint32_t);
@@ -616,6 +621,13 @@ BS_API bs_status bs_index_build_codebook(bs_index* ix, uint32_t seed, const char
                 (e = cudaMemcpy(host.data(), d_stage, cnt * row_slots * 4, cudaMemcpyDeviceToHost)) != cudaSuccess) {
                 cleanup();
                 return cuda_fail(e, "codebook rows");
+            }
+            // byte rows: put back the -0.0 values the byte copy dropped
+            const uint64_t lo = r0 * static_cast<uint64_t>(ix->dim), hi = lo + cnt * static_cast<uint64_t>(ix->dim);
+            for (auto it = std::lower_bound(ix->neg_zeros.begin(), ix->neg_zeros.end(), lo);
+                 it != ix->neg_zeros.end() && *it < hi; ++it) {
+                const uint64_t row = *it / static_cast<uint64_t>(ix->dim) - r0, d = *it % static_cast<uint64_t>(ix->dim);
+                host[static_cast<size_t>(row * row_slots + d)] = 0x80000000u;
             }
             ok = std::fwrite(host.data(), 4, cnt * row_slots, f) == cnt * row_slots;
         }

@@ -15,9 +15,11 @@
 // reference's output.
 //
 // Layout: one warp per node.  The warp rotates the node's row into shared
-// memory, then rotates up to 32 neighbour rows at once (each lane runs the
-// butterfly network of its own row, rows at an odd pitch so that the lanes
-// hit distinct banks) and each lane folds one edge.
+// memory, then up to 32 neighbour rows (k_quantize_edges_reg: each row's
+// butterfly network in registers across the lanes; k_quantize_edges, for
+// padded_dim above 1024: each lane runs the network of its own row in shared
+// memory), rows at an odd pitch so that the lanes hit distinct banks, and each
+// lane folds one edge.
 #include <cfloat>
 #include <cstdint>
 
@@ -31,8 +33,9 @@ namespace {
 __device__ __forceinline__ float elem(const float* p) { return __ldg(p); }
 __device__ __forceinline__ float elem(const uint8_t* p) { return static_cast<float>(__ldg(p)); }
 
-// In-place butterfly network over the n (power of two) floats x[0..n): stage len = 1, 2, ..., n/2 maps (a, b) at (i + j, i + j + len) to
-// (a + b, a - b) -- wht_inplace of the reference, one thread.
+// In-place butterfly network over the n (power of two) floats x[0..n): stage
+// len = 1, 2, ..., n/2 maps (a, b) at (i + j, i + j + len) to (a + b, a - b)
+// -- wht_inplace of the reference, one thread.
 __device__ __forceinline__ void wht_seq(float* x, uint32_t n) {
     for (uint32_t len = 1; len < n; len <<= 1)
         for (uint32_t i = 0; i < n; i += len << 1)
@@ -127,6 +130,141 @@ __global__ void __launch_bounds__(128) k_quantize_edges(CodebookArgs a, const T*
                         bin_sum += __popc(word);
                         codes[w] = word;
                     }
+                    fac_x0 = __fdiv_rn(fac_x0, r_norm);
+                    fac_x1 = __fmul_rn(fac_x1, fac_norm);
+                    float triple, dq;
+                    x87::edge_factors(r_norm, fac_x0, fac_x1, fac_norm, triple, dq);
+                    fac[i] = triple;
+                    fac[deg + i] = dq;
+                    fac[2u * deg + i] = __fmul_rn(dq, static_cast<float>(2 * bin_sum - static_cast<int>(dim)));
+                }
+            }
+            __syncwarp();   // the batch rows are rewritten next
+        }
+    }
+}
+
+// The network over one row of pdim = 32 * EPL components held in registers,
+// component lane + 32 k in x[k]: stages len = 1..16 pair lane with lane ^ len
+// (shuffles), stages len = 32, 64, ... pair x[k] with x[k | len / 32] in the
+// lane.  Stages run in the network's order and each element gets the same
+// operation as in wht_inplace (the lower one a + b, the upper one a - b), so
+// the bits are the same.
+template <int EPL>
+__device__ __forceinline__ void wht_lanes(float (&x)[EPL], unsigned lane) {
+#pragma unroll
+    for (int len = 1; len < 32; len <<= 1) {
+        const bool upper = (lane & static_cast<unsigned>(len)) != 0u;
+#pragma unroll
+        for (int k = 0; k < EPL; ++k) {
+            const float p = __shfl_xor_sync(dev::kFull, x[k], len);
+            x[k] = upper ? __fsub_rn(p, x[k]) : __fadd_rn(x[k], p);
+        }
+    }
+#pragma unroll
+    for (int m = 1; m < EPL; m <<= 1)
+#pragma unroll
+        for (int k = 0; k < EPL; ++k)
+            if (!(k & m)) {
+                const float a = x[k], b = x[k | m];
+                x[k] = __fadd_rn(a, b);
+                x[k | m] = __fsub_rn(a, b);
+            }
+}
+
+// signs * row (components past dim are +0.0, as the reference's rotate_vector)
+template <typename T, int EPL>
+__device__ __forceinline__ void load_rotated(const T* row, uint32_t dim, const float (&sg)[EPL], unsigned lane,
+                                             float (&x)[EPL]) {
+#pragma unroll
+    for (int k = 0; k < EPL; ++k) {
+        const uint32_t d = lane + 32u * static_cast<uint32_t>(k);
+        x[k] = d < dim ? __fmul_rn(elem(row + d), sg[k]) : 0.0f;
+    }
+}
+
+// k_quantize_edges with the butterfly networks in registers (pdim <= 1024,
+// 32 rows per batch): the warp rotates two neighbour rows at a time and
+// stores them at the odd pitch; each lane then folds its edge in one pass
+// (sqr_r, the code bits, fac_x0 and fac_x1 are independent sequential folds).
+template <typename T, int EPL>
+__global__ void __launch_bounds__(128) k_quantize_edges_reg(CodebookArgs a, const T* __restrict__ vecs) {
+    extern __shared__ __align__(16) float cb_smem[];
+    constexpr uint32_t pdim = 32u * EPL, wpp = EPL, pitch = pdim + 1u;
+    const unsigned lane = threadIdx.x & 31u;
+    const uint32_t dim = a.dim, deg = a.degree;
+    float* urot = cb_smem + static_cast<size_t>(threadIdx.x >> 5) * a.smem_floats_per_warp;
+    float* rows = urot + pdim;
+    const uint64_t warp = (static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const uint64_t nwarps = (static_cast<uint64_t>(gridDim.x) * blockDim.x) >> 5;
+    const float fac_norm = __fdiv_rn(1.0f, __fsqrt_rn(static_cast<float>(dim)));
+    float sg[EPL];
+#pragma unroll
+    for (int k = 0; k < EPL; ++k) sg[k] = a.signs[lane + 32u * k];
+
+    for (uint64_t u = warp; u < a.n; u += nwarps) {
+        {
+            float x[EPL];
+            load_rotated<T, EPL>(vecs + u * a.row_stride, dim, sg, lane, x);
+            wht_lanes<EPL>(x, lane);
+#pragma unroll
+            for (int k = 0; k < EPL; ++k) urot[lane + 32u * k] = x[k];
+        }
+        const uint32_t* arow = a.adj + u * deg;
+        for (uint32_t b0 = 0; b0 < deg; b0 += 32u) {
+            const uint32_t nb = deg - b0 < 32u ? deg - b0 : 32u;
+            const uint32_t myv = lane < nb ? arow[b0 + lane] : 0xffffffffu;
+            for (uint32_t r = 0; r < nb; r += 2) {
+                const uint32_t v0 = __shfl_sync(dev::kFull, myv, static_cast<int>(r));
+                const uint32_t v1 = __shfl_sync(dev::kFull, myv, static_cast<int>((r + 1u) & 31u));
+                const bool has1 = r + 1u < nb;
+                float x0[EPL], x1[EPL];
+                if (v0 < a.n) load_rotated<T, EPL>(vecs + static_cast<uint64_t>(v0) * a.row_stride, dim, sg, lane, x0);
+                if (has1 && v1 < a.n)
+                    load_rotated<T, EPL>(vecs + static_cast<uint64_t>(v1) * a.row_stride, dim, sg, lane, x1);
+                if (v0 < a.n) {
+                    wht_lanes<EPL>(x0, lane);
+#pragma unroll
+                    for (int k = 0; k < EPL; ++k) rows[r * pitch + lane + 32u * k] = x0[k];
+                }
+                if (has1 && v1 < a.n) {
+                    wht_lanes<EPL>(x1, lane);
+#pragma unroll
+                    for (int k = 0; k < EPL; ++k) rows[(r + 1u) * pitch + lane + 32u * k] = x1[k];
+                }
+            }
+            __syncwarp();
+            if (lane < nb) {
+                const uint32_t i = b0 + lane;
+                uint32_t* codes = a.codes + (u * deg + i) * wpp;
+                float* fac = a.factors + u * 3u * deg;
+                if (myv >= a.n) {
+                    for (uint32_t w = 0; w < wpp; ++w) codes[w] = 0u;
+                    fac[i] = FLT_MAX;
+                    fac[deg + i] = 0.0f;
+                    fac[2u * deg + i] = 0.0f;
+                } else {
+                    const float* x = rows + lane * pitch;
+                    float sqr_r = 0.0f, fac_x0 = 0.0f, fac_x1 = 0.0f;
+                    int bin_sum = 0;
+                    for (uint32_t w = 0; w < wpp; ++w) {
+                        uint32_t word = 0;
+                        const uint32_t dend = (w + 1u) * 32u < dim ? (w + 1u) * 32u : dim;
+#pragma unroll 4
+                        for (uint32_t d = w * 32u; d < dend; ++d) {
+                            const float ud = urot[d];
+                            const float res = __fsub_rn(x[d], ud);
+                            sqr_r = __fadd_rn(sqr_r, __fmul_rn(res, res));
+                            const bool pos = res > 0.0f;
+                            word |= (pos ? 1u : 0u) << (d & 31u);
+                            const float sv = pos ? 1.0f : -1.0f;
+                            fac_x0 = __fadd_rn(fac_x0, __fmul_rn(__fmul_rn(res, sv), fac_norm));
+                            fac_x1 = __fadd_rn(fac_x1, __fmul_rn(ud, sv));
+                        }
+                        bin_sum += __popc(word);
+                        codes[w] = word;
+                    }
+                    const float r_norm = __fadd_rn(__fsqrt_rn(sqr_r), 1e-10f);
                     fac_x0 = __fdiv_rn(fac_x0, r_norm);
                     fac_x1 = __fmul_rn(fac_x1, fac_norm);
                     float triple, dq;
@@ -325,8 +463,47 @@ cudaError_t medoid_impl(const T* vecs, uint64_t n, uint32_t dim, uint32_t row_st
     return cudaGetLastError();
 }
 
+template <typename T, int EPL>
+cudaError_t quantize_reg_impl(const CodebookArgs& a0, const T* vecs, size_t smem_optin, int num_sms,
+                              cudaStream_t stream) {
+    CodebookArgs a = a0;
+    const size_t floats = a.pdim + 32u * (a.pdim + 1u);
+    a.batch_rows = 32;
+    a.smem_floats_per_warp = static_cast<uint32_t>((floats + 3u) & ~static_cast<size_t>(3));
+    const size_t per_warp = static_cast<size_t>(a.smem_floats_per_warp) * 4u;
+    int warps = static_cast<int>(smem_optin / per_warp);
+    if (warps > 4) warps = 4;
+    if (warps < 1) return cudaErrorInvalidValue;
+    const size_t smem = per_warp * static_cast<size_t>(warps);
+    auto fn = k_quantize_edges_reg<T, EPL>;
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    int per_sm = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, 32 * warps, smem);
+    if (e != cudaSuccess) return e;
+    if (per_sm < 1) return cudaErrorInvalidConfiguration;
+    const uint64_t want = (a.n + warps - 1) / warps;
+    const uint64_t cap = static_cast<uint64_t>(per_sm) * num_sms;
+    const unsigned grid = static_cast<unsigned>(want < cap ? want : cap);
+    fn<<<grid, 32 * warps, smem, stream>>>(a, vecs);
+    return cudaGetLastError();
+}
+
 template <typename T>
 cudaError_t quantize_impl(const CodebookArgs& a0, const T* vecs, size_t smem_optin, int num_sms, cudaStream_t stream) {
+    // registers hold the butterfly networks up to pdim 1024 (32 rows per
+    // batch must fit the shared memory); the generic kernel otherwise
+    if ((a0.pdim + 32u * (a0.pdim + 1u)) * 4u <= smem_optin) {
+        switch (a0.pdim) {
+            case 32: return quantize_reg_impl<T, 1>(a0, vecs, smem_optin, num_sms, stream);
+            case 64: return quantize_reg_impl<T, 2>(a0, vecs, smem_optin, num_sms, stream);
+            case 128: return quantize_reg_impl<T, 4>(a0, vecs, smem_optin, num_sms, stream);
+            case 256: return quantize_reg_impl<T, 8>(a0, vecs, smem_optin, num_sms, stream);
+            case 512: return quantize_reg_impl<T, 16>(a0, vecs, smem_optin, num_sms, stream);
+            case 1024: return quantize_reg_impl<T, 32>(a0, vecs, smem_optin, num_sms, stream);
+            default: break;
+        }
+    }
     CodebookArgs a = a0;
     const size_t row_floats = a.pdim + 1u;
     // rows per batch: up to 32, within the opt-in shared memory of one warp

@@ -137,6 +137,7 @@ class ClockSampler:
         self.proc = None
         self.lines = []
         self.t = None
+        self.in_region = 0
 
     def __enter__(self):
         try:
@@ -160,6 +161,13 @@ class ClockSampler:
             self.lines.append(line.strip())
 
     def __exit__(self, *exc):
+        self.in_region = len(self.lines)
+        if self.proc and not self.lines:
+            # a timed region shorter than the sampling interval: take the
+            # first sample after it (labelled in the summary)
+            t0 = time.time()
+            while not self.lines and time.time() - t0 < 0.5:
+                time.sleep(0.005)
         if self.proc:
             self.proc.terminate()
             try:
@@ -184,8 +192,11 @@ class ClockSampler:
             for nm, v in zip(names, parts[5:9]):
                 if v.lower() == "active":
                     reasons.add(nm)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        out = {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+               "reasons": sorted(reasons), "samples": len(sm)}
+        if sm and not getattr(self, "in_region", 1):
+            out["window"] = "first sample after the timed region (region shorter than the 20 ms interval)"
+        return out
 
 
 def c2_data(nq_total: int):
