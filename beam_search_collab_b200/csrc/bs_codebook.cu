@@ -23,6 +23,7 @@
 #include <cfloat>
 #include <cstdint>
 
+#include "bs_centroid.cuh"
 #include "bs_device.cuh"
 #include "bs_internal.h"
 #include "bs_x87.hpp"
@@ -281,60 +282,6 @@ __global__ void __launch_bounds__(128) k_quantize_edges_reg(CodebookArgs a, cons
 
 // --- medoid -----------------------------------------------------------------
 
-constexpr uint32_t kMedoidDimsPerThread = 4;
-
-// centroid[d] = (sum over rows 0..n-1 in order of (double)row[d]) / n, rows
-// streamed through shared memory in double-buffered tiles (cp.async); thread t
-// folds dimensions t, t + blockDim, ...
-template <typename T>
-__global__ void k_medoid_centroid(const T* __restrict__ vecs, uint64_t n, uint32_t dim, uint32_t row_stride,
-                                  uint32_t tile_rows, double* __restrict__ centroid) {
-    extern __shared__ __align__(16) unsigned char tiles[];
-    const uint32_t row_bytes = row_stride * static_cast<uint32_t>(sizeof(T));
-    const uint32_t tile_bytes = tile_rows * row_bytes;
-    const unsigned char* src = reinterpret_cast<const unsigned char*>(vecs);
-    const uint64_t ntiles = (n + tile_rows - 1) / tile_rows;
-    auto load = [&](uint64_t t) {
-        if (t < ntiles) {
-            const uint64_t r0 = t * tile_rows;
-            const uint64_t rows = n - r0 < tile_rows ? n - r0 : tile_rows;
-            const uint32_t pieces = static_cast<uint32_t>(rows * row_bytes / 16u);
-            unsigned char* dst = tiles + (t & 1u) * tile_bytes;
-            const unsigned char* s = src + r0 * row_bytes;
-            for (uint32_t i = threadIdx.x; i < pieces; i += blockDim.x) dev::cp_async16(dst + 16u * i, s + 16u * i);
-        }
-        asm volatile("cp.async.commit_group;\n" ::: "memory");
-    };
-    double acc[kMedoidDimsPerThread];
-#pragma unroll
-    for (uint32_t k = 0; k < kMedoidDimsPerThread; ++k) acc[k] = 0.0;
-    load(0);
-    for (uint64_t t = 0; t < ntiles; ++t) {
-        load(t + 1);
-        asm volatile("cp.async.wait_group 1;\n" ::: "memory");
-        __syncthreads();
-        const uint32_t rows = static_cast<uint32_t>(n - t * tile_rows < tile_rows ? n - t * tile_rows : tile_rows);
-        const T* tile = reinterpret_cast<const T*>(tiles + (t & 1u) * tile_bytes);
-#pragma unroll
-        for (uint32_t k = 0; k < kMedoidDimsPerThread; ++k) {
-            const uint32_t d = threadIdx.x + k * blockDim.x;
-            if (d < dim) {
-                double c = acc[k];
-#pragma unroll 8
-                for (uint32_t r = 0; r < rows; ++r)
-                    c = __dadd_rn(c, static_cast<double>(static_cast<float>(tile[r * row_stride + d])));
-                acc[k] = c;
-            }
-        }
-        __syncthreads();
-    }
-#pragma unroll
-    for (uint32_t k = 0; k < kMedoidDimsPerThread; ++k) {
-        const uint32_t d = threadIdx.x + k * blockDim.x;
-        if (d < dim) centroid[d] = __ddiv_rn(acc[k], static_cast<double>(n));
-    }
-}
-
 __device__ __forceinline__ bool medoid_less(double a, uint32_t ia, double b, uint32_t ib) {
     return a < b || (a == b && ia < ib);
 }
@@ -438,20 +385,11 @@ cudaError_t medoid_impl(const T* vecs, uint64_t n, uint32_t dim, uint32_t row_st
     double* bdist = centroid + ((dim + 1u) & ~1u);
     uint32_t* bidx = reinterpret_cast<uint32_t*>(bdist + blocks);
     const uint32_t row_bytes = row_stride * static_cast<uint32_t>(sizeof(T));
-    if (dim > 1024u * kMedoidDimsPerThread || row_bytes % 16u != 0 || (reinterpret_cast<uintptr_t>(vecs) & 15u) != 0)
+    cudaError_t e = cudaSuccess;
+    if (!launch_centroid_sliced<T, double, FoldF64>(vecs, n, dim, row_bytes, FoldF64{static_cast<double>(n)}, centroid,
+                                                    stream, e))
         return cudaErrorInvalidValue;
-    uint32_t threads = (dim + kMedoidDimsPerThread - 1) / kMedoidDimsPerThread;
-    threads = (threads + 31u) & ~31u;
-    if (threads < 256u) threads = 256u;
-    if (threads > 1024u) threads = 1024u;
-    const uint64_t want = (48u * 1024u) / row_bytes;
-    const uint32_t tile_rows = static_cast<uint32_t>(want < 1 ? 1 : (want < n ? want : n));
-    const size_t smem = 2ull * tile_rows * row_bytes;
-    cudaError_t e = cudaFuncSetAttribute(k_medoid_centroid<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    k_medoid_centroid<T><<<1, threads, smem, stream>>>(vecs, n, dim, row_stride, tile_rows, centroid);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
     const size_t csm = static_cast<size_t>(dim) * sizeof(double);
     if (csm > 48u * 1024u) {
         e = cudaFuncSetAttribute(k_medoid_nearest<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(csm));

@@ -5,7 +5,8 @@
 //   inv = 1/n;  centroid[d] = sum over rows i = 0..n-1 (in order) of row_i[d]*inv
 //   entry = first row with the smallest sequential squared distance to it.
 // The centroid sum is a sequential fold per dimension, so one thread owns
-// one dimension and walks the rows in order (coalesced across threads); the
+// one dimension and walks the rows in order (bs_centroid.cuh: one block per
+// 32-byte slice of the rows, streamed through shared memory); the
 // per-row distances are independent, one thread per row, folded over d in
 // order; the argmin packs (distance, row) into one 64-bit key so that
 // atomicMin keeps the smallest distance and, among equals, the first row.
@@ -14,6 +15,7 @@
 #include <cfloat>
 #include <cstdint>
 
+#include "bs_centroid.cuh"
 #include "bs_device.cuh"
 #include "bs_internal.h"
 
@@ -40,62 +42,6 @@ __global__ void k_centroid(const T* __restrict__ vecs, uint64_t n, uint32_t dim,
     }
     for (; i < n; ++i) c = __fadd_rn(c, __fmul_rn(load_elem(p + i * row_stride), inv));
     centroid[d] = c;
-}
-
-// The same fold with the rows streamed through shared memory: the whole
-// block copies tiles of rows with cp.async (double-buffered, many rows in
-// flight), and thread t folds dimensions t, t + blockDim, ... over each
-// tile's rows in order -- the same operations in the same order as
-// k_centroid, so the same bits, without one global round trip per few rows.
-constexpr uint32_t kCentroidDimsPerThread = 4;
-
-template <typename T>
-__global__ void k_centroid_tiled(const T* __restrict__ vecs, uint64_t n, uint32_t dim, uint32_t row_stride,
-                                 float inv, uint32_t tile_rows, float* __restrict__ centroid) {
-    extern __shared__ __align__(16) unsigned char tiles[];
-    const uint32_t row_bytes = row_stride * static_cast<uint32_t>(sizeof(T));
-    const uint32_t tile_bytes = tile_rows * row_bytes;
-    const unsigned char* src = reinterpret_cast<const unsigned char*>(vecs);
-    const uint64_t ntiles = (n + tile_rows - 1) / tile_rows;
-    auto load = [&](uint64_t t) {
-        if (t < ntiles) {
-            const uint64_t r0 = t * tile_rows;
-            const uint64_t rows = n - r0 < tile_rows ? n - r0 : tile_rows;
-            const uint32_t pieces = static_cast<uint32_t>(rows * row_bytes / 16u);
-            unsigned char* dst = tiles + (t & 1u) * tile_bytes;
-            const unsigned char* s = src + r0 * row_bytes;
-            for (uint32_t i = threadIdx.x; i < pieces; i += blockDim.x) dev::cp_async16(dst + 16u * i, s + 16u * i);
-        }
-        asm volatile("cp.async.commit_group;\n" ::: "memory");
-    };
-    float acc[kCentroidDimsPerThread];
-#pragma unroll
-    for (uint32_t k = 0; k < kCentroidDimsPerThread; ++k) acc[k] = 0.0f;
-    load(0);
-    for (uint64_t t = 0; t < ntiles; ++t) {
-        load(t + 1);
-        asm volatile("cp.async.wait_group 1;\n" ::: "memory");
-        __syncthreads();
-        const uint32_t rows = static_cast<uint32_t>(n - t * tile_rows < tile_rows ? n - t * tile_rows : tile_rows);
-        const T* tile = reinterpret_cast<const T*>(tiles + (t & 1u) * tile_bytes);
-#pragma unroll
-        for (uint32_t k = 0; k < kCentroidDimsPerThread; ++k) {
-            const uint32_t d = threadIdx.x + k * blockDim.x;
-            if (d < dim) {
-                float c = acc[k];
-#pragma unroll 8
-                for (uint32_t r = 0; r < rows; ++r)
-                    c = __fadd_rn(c, __fmul_rn(static_cast<float>(tile[r * row_stride + d]), inv));
-                acc[k] = c;
-            }
-        }
-        __syncthreads();   // this buffer is refilled by the next iteration's load
-    }
-#pragma unroll
-    for (uint32_t k = 0; k < kCentroidDimsPerThread; ++k) {
-        const uint32_t d = threadIdx.x + k * blockDim.x;
-        if (d < dim) centroid[d] = acc[k];
-    }
 }
 
 template <typename T>
@@ -140,19 +86,8 @@ cudaError_t entry_impl(const T* vecs, uint64_t n, uint32_t dim, uint32_t row_str
     if (e != cudaSuccess) return e;
     const float inv = 1.0f / static_cast<float>(n);
     const uint32_t row_bytes = row_stride * static_cast<uint32_t>(sizeof(T));
-    if (dim <= 1024u * kCentroidDimsPerThread && row_bytes % 16u == 0 &&
-        (reinterpret_cast<uintptr_t>(vecs) & 15u) == 0) {
-        uint32_t threads = (dim + kCentroidDimsPerThread - 1) / kCentroidDimsPerThread;
-        threads = (threads + 31u) & ~31u;
-        if (threads < 256u) threads = 256u;
-        if (threads > 1024u) threads = 1024u;
-        const uint64_t want = (48u * 1024u) / row_bytes;
-        const uint32_t tile_rows = static_cast<uint32_t>(want < 1 ? 1 : (want < n ? want : n));
-        const size_t smem = 2ull * tile_rows * row_bytes;
-        e = cudaFuncSetAttribute(k_centroid_tiled<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(smem));
+    if (launch_centroid_sliced<T, float, FoldF32>(vecs, n, dim, row_bytes, FoldF32{inv}, centroid, stream, e)) {
         if (e != cudaSuccess) return e;
-        k_centroid_tiled<T><<<1, threads, smem, stream>>>(vecs, n, dim, row_stride, inv, tile_rows, centroid);
     } else {
         k_centroid<T><<<(dim + 127) / 128, 128, 0, stream>>>(vecs, n, dim, row_stride, inv, centroid);
     }
