@@ -68,7 +68,9 @@ def test_search_on_built_codebook_matches_golden(name):
 @pytest.mark.parametrize("seed", [12345, 7])
 def test_byte_valued_rows_match_reference_tool(storage, seed, tmp_path, monkeypatch):
     """i128 rows are integers in [0, 255]: the index keeps a byte copy unless
-    f32 storage is forced; both must give the reference tool's file."""
+    f32 storage is forced; both must give the reference tool's file.  The
+    base holds -0.0 values (rounded negatives), which the byte copy drops and
+    the writer restores from the positions the index kept."""
     g = G.load("i128")
     ref = _ref_codebook(g.files["base"], g.files["graph"], str(tmp_path / "ref.bin"), seed)
     if storage == "f32":
