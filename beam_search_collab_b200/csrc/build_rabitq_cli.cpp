@@ -10,6 +10,7 @@
 #include <chrono>
 #include <cstdint>
 #include <cstdio>
+#include <cstdlib>
 #include <iostream>
 #include <string>
 
@@ -32,6 +33,9 @@ int main(int argc, char** argv) {
                   << " [-seed <uint32>]\n";
         return 1;
     }
+    // the builder never searches: no neighbourhood blocks (rows repeated per
+    // node for the search kernel, 25 GB for a 1M-node degree-64 graph)
+    setenv("BSEARCH_LAYOUT", "gather", 0);
     bs_index* index = nullptr;
     if (bs_index_load(graph_file.c_str(), base_file.c_str(), device, &index) != BS_OK) {
         std::cerr << "Error: " << bs_last_error() << "\n";
