@@ -17,6 +17,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <initializer_list>
 #include <mutex>
 #include <random>
 #include <string>
@@ -59,6 +60,9 @@ struct bs_index {
     uint32_t* d_codes = nullptr;
     float* d_factors = nullptr;
     float* d_signs = nullptr;
+    // error word every search kernel on this index ORs its error bits into
+    // (read and cleared by bs_index_take_errors)
+    unsigned int* d_err = nullptr;
     // cached centroid-nearest entry
     std::mutex mu;
     bool entry_valid = false;
@@ -98,15 +102,31 @@ struct DeviceGuard {
     }
 };
 
-// true: device (or managed) memory usable by kernels on `device`.
-bool is_device_ptr(const void* ptr) {
-    if (!ptr) return false;
+// Where a buffer lives, seen from `device`.
+enum PtrKind { kHostPtr = 0, kThisDevice = 1, kOtherDevice = 2 };
+
+PtrKind pointer_kind(const void* ptr, int device) {
+    if (!ptr) return kHostPtr;
     cudaPointerAttributes a;
     if (cudaPointerGetAttributes(&a, ptr) != cudaSuccess) {
         cudaGetLastError();   // clear the sticky-free error of an unknown pointer
-        return false;
+        return kHostPtr;
     }
-    return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+    if (a.type == cudaMemoryTypeManaged) return kThisDevice;   // reachable from every device
+    if (a.type == cudaMemoryTypeDevice) return a.device == device ? kThisDevice : kOtherDevice;
+    return kHostPtr;
+}
+
+// true: device memory usable by kernels on `device` (its own memory, or
+// managed memory).
+bool is_device_ptr(const void* ptr, int device) { return pointer_kind(ptr, device) == kThisDevice; }
+
+// Device memory of another GPU given to a search on `device`: kernels would
+// read it across the bus (or fault without peer access), so it is refused.
+bool any_foreign(int device, std::initializer_list<const void*> ptrs) {
+    for (const void* p : ptrs)
+        if (p && pointer_kind(p, device) == kOtherDevice) return true;
+    return false;
 }
 
 // Page-locked host memory that `device`'s context has mapped: the device
@@ -333,6 +353,9 @@ void fill_params(const bs_index* ix, const ModeInfo& mi, const bs_search_params*
         p.team_qhi = std::min(p.team_qhi, 255.0f);
     }
     if (force_seq()) { p.team_qlo = 1.0f; p.team_qhi = 0.0f; }
+    p.sticky_err = ix->d_err;
+    p.wait_polls = bsb::kDefaultWaitPolls;
+    if (const char* w = std::getenv("BSEARCH_WAIT_POLLS")) p.wait_polls = static_cast<uint32_t>(std::strtoul(w, nullptr, 10));
     shape = LaunchShape{};
     if (ix->u8) shape.dmode = bsb::kU8;
     else shape.dmode = p.team_qlo <= p.team_qhi ? bsb::kTeam : bsb::kSeq;
@@ -350,6 +373,7 @@ void free_index(bs_index* ix) {
     cudaFree(ix->d_codes);
     cudaFree(ix->d_factors);
     cudaFree(ix->d_signs);
+    cudaFree(ix->d_err);
     delete ix;
 }
 
@@ -434,6 +458,10 @@ BS_API bs_status bs_index_create(const bs_graph_desc* desc, int device, bs_index
     ix->row_bytes = (static_cast<uint32_t>(desc->dim) + 15u) & ~15u;
 
     const size_t ebytes = static_cast<size_t>(ix->n) * ix->degree * sizeof(uint32_t);
+    if ((e = cudaMalloc(&ix->d_err, 256)) != cudaSuccess || (e = cudaMemset(ix->d_err, 0, 256)) != cudaSuccess) {
+        free_index(ix);
+        return cuda_fail(e, "error word");
+    }
     if ((e = cudaMalloc(&ix->d_adj, ebytes)) != cudaSuccess) { free_index(ix); return cuda_fail(e, "adjacency"); }
     if (ix->u8) {
         const size_t vbytes = static_cast<size_t>(ix->n) * ix->row_bytes;
@@ -680,6 +708,20 @@ BS_API bs_status bs_index_rabitq_entry(const bs_index* ix, uint32_t* entry) {
     return BS_OK;
 }
 
+BS_API bs_status bs_index_take_errors(bs_index* ix, void* stream_, uint32_t* flags) {
+    if (!ix || !flags) return fail(BS_ERR_INVALID_ARGUMENT, "index or flags is NULL");
+    DeviceGuard g(ix->device);
+    if (!g.ok) return fail(BS_ERR_CUDA, "cannot select device %d", ix->device);
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+    unsigned int h = 0;
+    cudaError_t e = cudaMemcpyAsync(&h, ix->d_err, sizeof(h), cudaMemcpyDeviceToHost, stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(ix->d_err, 0, sizeof(h), stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    if (e != cudaSuccess) return cuda_fail(e, "error word");
+    *flags = h;
+    return BS_OK;
+}
+
 BS_API void bs_index_destroy(bs_index* ix) { free_index(ix); }
 
 BS_API bs_status bs_search(bs_index* ix, const bs_search_params* prm, const float* queries, uint32_t nq,
@@ -728,9 +770,11 @@ BS_API bs_status bs_search(bs_index* ix, const bs_search_params* prm, const floa
     if (nq == 0) return BS_OK;
 
     cudaError_t e0 = cudaSuccess;
-    const bool q_dev = is_device_ptr(queries);
-    const bool i_dev = is_device_ptr(ids);
-    const bool d_dev = dists ? is_device_ptr(dists) : true;
+    if (any_foreign(ix->device, {queries, ids, dists}))
+        return fail(BS_ERR_INVALID_ARGUMENT, "a buffer lives on another GPU than the index (device %d)", ix->device);
+    const bool q_dev = is_device_ptr(queries, ix->device);
+    const bool i_dev = is_device_ptr(ids, ix->device);
+    const bool d_dev = dists ? is_device_ptr(dists, ix->device) : true;
     // Host buffers that are page-locked and mapped into this device's
     // context are used in place: each warp reads its query over the bus when
     // it starts it and writes its result row back when it ends, so the
@@ -875,7 +919,10 @@ BS_API bs_status bs_search_no_alloc(bs_index* ix, const bs_search_params* prm, c
 
     DeviceGuard g(ix->device);
     if (!g.ok) return fail(BS_ERR_CUDA, "cannot select device %d", ix->device);
-    if (nq > 0 && (!is_device_ptr(queries) || !is_device_ptr(ids) || (dists && !is_device_ptr(dists))))
+    if (nq > 0 && any_foreign(ix->device, {queries, ids, dists}))
+        return fail(BS_ERR_INVALID_ARGUMENT, "a buffer lives on another GPU than the index (device %d)", ix->device);
+    if (nq > 0 && (!is_device_ptr(queries, ix->device) || !is_device_ptr(ids, ix->device) ||
+                   (dists && !is_device_ptr(dists, ix->device))))
         return fail(BS_ERR_INVALID_ARGUMENT,
                     "bs_search_no_alloc takes device pointers only (host buffers would need staging memory)");
     cudaStream_t stream = static_cast<cudaStream_t>(stream_);
@@ -940,12 +987,13 @@ BS_API bs_status bs_merge_shards(const float* dists, const uint32_t* ids, uint32
         return fail(BS_ERR_INVALID_ARGUMENT, "need 0 < K_out <= shards * K");
     if (!id_offsets) return fail(BS_ERR_INVALID_ARGUMENT, "id_offsets is NULL");
     if (nq == 0) return BS_OK;
-    if (!is_device_ptr(dists) || !is_device_ptr(ids) || !is_device_ptr(out_ids) ||
-        (out_dists && !is_device_ptr(out_dists)))
-        return fail(BS_ERR_INVALID_ARGUMENT, "bs_merge_shards takes device pointers");
     int dev = 0, sms = 0;
     cudaError_t e = cudaGetDevice(&dev);
-    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return cuda_fail(e, "device query");
+    if (!is_device_ptr(dists, dev) || !is_device_ptr(ids, dev) || !is_device_ptr(out_ids, dev) ||
+        (out_dists && !is_device_ptr(out_dists, dev)))
+        return fail(BS_ERR_INVALID_ARGUMENT, "bs_merge_shards takes device pointers on the current device");
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) return cuda_fail(e, "device query");
     bsb::MergeArgs a{};
     a.dists = dists;

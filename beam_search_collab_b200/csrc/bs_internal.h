@@ -50,7 +50,13 @@ enum ErrorFlag : unsigned int {
     kErrProbeBound = 1u,     // a visited-table probe ran the whole table
     kErrSpillFull = 2u,      // a query overflowed its RaBitQ spill table
     kErrWaitTimeout = 4u,    // a bulk-copy wait hit its iteration bound
+    kErrCopyPending = 8u,    // ... and the copy in flight did not land either
 };
+
+// Polls of a bulk-copy wait before it gives up (each mbarrier.try_wait may
+// itself suspend the warp for a while).  BSEARCH_WAIT_POLLS overrides it for
+// the first wait of an expansion: a test sets 0 to drive the timeout path.
+constexpr unsigned kDefaultWaitPolls = 1u << 22;
 
 // Everything a search launch needs, passed by value.
 struct SearchParams {
@@ -121,7 +127,20 @@ struct SearchParams {
     float* out_dists;           // [nq][K] or null
     uint32_t* q_stats;          // [nq][2] (expansions, distances) or null
     DevCounters* counters;
+    // the index's error word: every kernel ORs its error bits into it too, so
+    // a caller of an asynchronous search can collect them later
+    unsigned int* sticky_err;
+    uint32_t wait_polls;        // first bounded wait of an expansion (polls)
 };
+
+#ifdef __CUDACC__
+// One lane reports a warp's error bits: to the call's counters and to the
+// index's error word.
+__device__ __forceinline__ void report_errors(const SearchParams& p, unsigned err) {
+    atomicOr(&p.counters->error_flags, err);
+    if (p.sticky_err) atomicOr(p.sticky_err, err);
+}
+#endif
 
 struct LaunchShape {
     int regx;                   // beam registers per lane (beam capacity 32*regx)

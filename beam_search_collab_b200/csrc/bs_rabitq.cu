@@ -311,7 +311,7 @@ __global__ void __launch_bounds__(128, (RX <= 8 ? 5 : 2)) k_search_rabitq(const 
         }
         __syncwarp();
     }
-    if (lane == 0 && err) atomicOr(&p.counters->error_flags, err);
+    if (lane == 0 && err) report_errors(p, err);
 }
 
 using KernelFn = void (*)(SearchParams);

@@ -210,7 +210,7 @@ __global__ void __launch_bounds__(256) k_search_l2(const SearchParams p) {
         }
         __syncwarp();
     }
-    if (lane == 0 && err) atomicOr(&p.counters->error_flags, err);
+    if (lane == 0 && err) report_errors(p, err);
 }
 
 using KernelFn = void (*)(SearchParams);

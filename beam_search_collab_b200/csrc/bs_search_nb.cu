@@ -83,13 +83,11 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* mbar, unsigned phase) {
     return ok != 0;
 }
 
-// Bounded wait: every lane polls at most kMaxPolls times (each try_wait may
+// Bounded wait: every lane polls at most `polls` times (each try_wait may
 // itself suspend for a while); the warp agrees on the outcome.
-constexpr unsigned kMaxPolls = 1u << 22;
-
-__device__ __forceinline__ bool mbar_wait(uint64_t* mbar, unsigned phase) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* mbar, unsigned phase, unsigned polls) {
     bool done = false;
-    for (unsigned i = 0; i < kMaxPolls && !done; ++i) done = mbar_try_wait(mbar, phase);
+    for (unsigned i = 0; i < polls && !done; ++i) done = mbar_try_wait(mbar, phase);
     return __all_sync(kFull, done);
 }
 
@@ -286,11 +284,12 @@ __global__ void __launch_bounds__(256) k_search_nb(const SearchParams p) {
                 // candidate turns up: start it towards L2 now
                 if (nxt != kNoNode) bulk_prefetch_l2(p.nb + static_cast<size_t>(nxt) * p.nb_stride, p.nb_stride);
             }
-            if (!mbar_wait(mbar, phase)) {
-                // give the copy in flight a last bounded chance, then leave:
-                // the host reads the flag and reports BS_ERR_KERNEL
-                mbar_wait(mbar, phase);
-                if (lane == 0) atomicOr(&p.counters->error_flags, err | kErrWaitTimeout);
+            if (!mbar_wait(mbar, phase, p.wait_polls)) {
+                // wait (bounded again) for the copy in flight to land before
+                // leaving, so that no copy outlives the warp; the host reads
+                // the flag and reports BS_ERR_KERNEL
+                const bool landed = mbar_wait(mbar, phase, kDefaultWaitPolls);
+                if (lane == 0) report_errors(p, err | kErrWaitTimeout | (landed ? 0u : kErrCopyPending));
                 return;
             }
             phase ^= 1u;
@@ -403,7 +402,7 @@ __global__ void __launch_bounds__(256) k_search_nb(const SearchParams p) {
         }
         __syncwarp();
     }
-    if (lane == 0 && err) atomicOr(&p.counters->error_flags, err);
+    if (lane == 0 && err) report_errors(p, err);
 }
 
 // One warp per node: the node's adjacency row (a repeated id replaced by

@@ -11,8 +11,12 @@
 // ["Loaded rabitq codebook: ..."], "  time: X ms  qps: Y" (mean of 5 launches,
 // wall clock, queries already on the device), ["  duplicates: ..."],
 // "recall@K: R".  An optional "print_stats": true in "search" adds one
-// "  stats: ..." line with the search counters.
+// "  stats: ..." line with the search counters; an optional "results" path in
+// "data" receives the result ids as raw uint32 [nq][K] (BS_NO_NODE past the
+// end of the beam).  Neither key exists in the reference; both are ignored
+// by it.
 #include <chrono>
+#include <cstdio>
 #include <cstdint>
 #include <iostream>
 #include <iterator>
@@ -90,6 +94,7 @@ int main() {
         const std::string query_file = need("query");
         const std::string gt_file = need("gt");
         const std::string codebook_file = jd.value("codebook", std::string());
+        const std::string results_file = jd.value("results", std::string());
 
         // host copies (CPUGraph::load, include/cpu_graph.hpp:125-173)
         uint64_t n = 0, nv = 0, nq = 0, ngt = 0;
@@ -192,6 +197,12 @@ int main() {
         if (!check(bs_copy_to_host(index, h_results.data(), d_results, rbytes), "result download")) return 1;
         const float recall = compute_recall(h_results.data(), gt.data(), nq, K, gt_k);
         std::cout << "recall@" << K << ": " << recall << std::endl;
+        if (!results_file.empty()) {
+            std::FILE* f = std::fopen(results_file.c_str(), "wb");
+            const bool ok = f && std::fwrite(h_results.data(), sizeof(uint32_t), h_results.size(), f) == h_results.size();
+            if (f) std::fclose(f);
+            if (!ok) return die("Cannot write results: " + results_file);
+        }
 
         bs_device_free(index, d_queries);
         bs_device_free(index, d_results);

@@ -31,8 +31,15 @@ base and graph instead (one JSON line, edges/s; the reference build_rabitq on
 all host threads as the CPU baseline, and the two codebook files compared).
 
 Multi-GPU (torchrun, one rank per GPU): query sharding over a replicated
-index, no collective on the data path; every rank searches its own 10,000
-queries (weak scaling); value = all ranks' queries / max-over-ranks time.
+index, no collective on the data path.  --scaling weak (default): every rank
+searches its own 10,000 queries; --scaling strong: the workload's 10,000
+queries are split over the ranks.  value = all ranks' queries / max-over-ranks
+time.
+
+Checks carried in the line: `parity` compares our rows with the reference CPU
+search's rows for the CPU-baseline sample (identical rows, distances, recall);
+`config.kernel_errors` holds the kernels' error bits from the timed launches
+(a non-zero value aborts the run).
 """
 from __future__ import annotations
 
@@ -126,77 +133,80 @@ def peaks():
     return 6650.0, "fallback"
 
 
-class ClockSampler:
-    """nvidia-smi clocks and throttle reasons during the timed region."""
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+def host_threads() -> int:
+    """Host threads this process may use (torchrun sets OMP_NUM_THREADS=1 for
+    its ranks; the CPU reference is given the affinity count explicitly)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.proc = None
-        self.lines = []
+
+class ClockSampler:
+    """SM clocks and throttle reasons sampled through NVML every millisecond
+    while the timed region runs (nvidia-smi's own loop samples every 20 ms at
+    best, too coarse for a timed region of a few milliseconds)."""
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+    def __init__(self, torch_device: int):
+        self.dev = torch_device
+        self.samples = []
+        self.stop = threading.Event()
         self.t = None
-        self.in_region = 0
+        self.h = None
+        self.smax = None
+        self.err = None
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "20"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
+            import pynvml
+            import torch
+            self.nv = pynvml
+            pynvml.nvmlInit()
+            try:
+                uuid = str(torch.cuda.get_device_properties(self.dev).uuid)
+                uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+                self.h = pynvml.nvmlDeviceGetHandleByUUID(uuid.encode())
+            except Exception:
+                vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+                idx = int(vis.split(",")[self.dev]) if vis else self.dev
+                self.h = pynvml.nvmlDeviceGetHandleByIndex(idx)
+            self.smax = float(pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM))
+            self.bits = (pynvml.nvmlClocksEventReasonHwSlowdown, pynvml.nvmlClocksEventReasonHwThermalSlowdown,
+                         pynvml.nvmlClocksEventReasonSwThermalSlowdown, pynvml.nvmlClocksEventReasonSwPowerCap)
+            self._sample()
+            self.samples.clear()
+            self.t = threading.Thread(target=self._run, daemon=True)
             self.t.start()
-            # nvidia-smi needs a moment to start: sample from before the timed
-            # region begins, not after it ended
-            t0 = time.time()
-            while not self.lines and time.time() - t0 < 5.0:
-                time.sleep(0.01)
-            self.lines.clear()
-        except Exception:
-            self.proc = None
+        except Exception as e:   # no NVML: the line says so
+            self.err = repr(e)
+            self.h = None
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+    def _sample(self):
+        sm = float(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+        rs = int(self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h))
+        self.samples.append((sm, rs))
+
+    def _run(self):
+        while not self.stop.is_set():
+            self._sample()
+            time.sleep(0.001)
 
     def __exit__(self, *exc):
-        self.in_region = len(self.lines)
-        if self.proc and not self.lines:
-            # a timed region shorter than the sampling interval: take the
-            # first sample after it (labelled in the summary)
-            t0 = time.time()
-            while not self.lines and time.time() - t0 < 0.5:
-                time.sleep(0.005)
-        if self.proc:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except Exception:
-                self.proc.kill()
         if self.t:
+            self.stop.set()
             self.t.join(timeout=2)
+            if not self.samples:
+                self._sample()
 
     def summary(self):
-        sm, smax, reasons = [], None, set()
-        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        for ln in self.lines:
-            parts = [x.strip() for x in ln.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                smax = float(parts[2])
-            except ValueError:
-                continue
-            for nm, v in zip(names, parts[5:9]):
-                if v.lower() == "active":
-                    reasons.add(nm)
-        out = {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
-               "reasons": sorted(reasons), "samples": len(sm)}
-        if sm and not getattr(self, "in_region", 1):
-            out["window"] = "first sample after the timed region (region shorter than the 20 ms interval)"
-        return out
+        if self.h is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0, "error": self.err}
+        sm = [a for a, _ in self.samples]
+        reasons = sorted({nm for _, r in self.samples for nm, b in zip(self.NAMES, self.bits) if r & b})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.smax, "reasons": reasons,
+                "samples": len(sm), "interval_ms": 1}
 
 
 def c2_data(nq_total: int):
@@ -241,6 +251,37 @@ def recall_at_k(pred, gt, k=K):
 
 # --------------------------------------------------------------- our arm
 
+def query_share(rank, world, strong):
+    """This rank's query range: weak scaling gives every rank its own
+    NQ_PER_GPU queries; strong scaling splits the workload's NQ_PER_GPU
+    queries over the ranks (contiguous ranges)."""
+    if not strong:
+        return rank * NQ_PER_GPU, (rank + 1) * NQ_PER_GPU
+    return rank * NQ_PER_GPU // world, (rank + 1) * NQ_PER_GPU // world
+
+
+def useful_distance_count(B, base, edges, queries, params, local_rank):
+    """Distances the reference search itself computes for these queries (one
+    per distinct pushed node): the gather-layout kernel with a visited table
+    that never resets counts exactly those (pinned against the CPU oracle by
+    the GPU tests).  Untimed; the block layout scores every row of a block."""
+    old = os.environ.get("BSEARCH_LAYOUT")
+    os.environ["BSEARCH_LAYOUT"] = "gather"
+    try:
+        gx = B.Index.from_arrays(base, edges, device=local_rank)
+    finally:
+        if old is None:
+            os.environ.pop("BSEARCH_LAYOUT")
+        else:
+            os.environ["BSEARCH_LAYOUT"] = old
+    try:
+        p = B.SearchParams(mode=params.mode, K=params.K, topk_size=params.topk_size, filter_capacity=1 << 15)
+        _, _, st = gx.search(queries, p, with_dists=False)
+        return st.distances, st.expansions
+    finally:
+        gx.close()
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
     import beam_search_collab_b200 as B
@@ -248,10 +289,15 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     cfg = CONFIGS[CFG_NAME]
+    strong = args.scaling == "strong"
     t0 = time.time()
-    base, queries_all, edges, codebook = config_data(CFG_NAME, NQ_PER_GPU * world)
-    queries = queries_all[rank * NQ_PER_GPU:(rank + 1) * NQ_PER_GPU]
-    log(f"[rank {rank}] data ready in {time.time() - t0:.1f}s: base {base.shape}, graph {edges.shape}")
+    base, queries_all, edges, codebook = config_data(CFG_NAME, NQ_PER_GPU * (1 if strong else world))
+    q0, q1 = query_share(rank, world, strong)
+    queries = np.ascontiguousarray(queries_all[q0:q1])
+    nq = len(queries)
+    nq_job = NQ_PER_GPU if strong else NQ_PER_GPU * world
+    log(f"[rank {rank}] data ready in {time.time() - t0:.1f}s: base {base.shape}, graph {edges.shape}, "
+        f"{nq} queries")
     ix = B.Index.from_arrays(base, edges, device=local_rank)
     if codebook:
         ix.load_codebook(codebook)
@@ -269,6 +315,8 @@ def run_ours(args, rank, world, local_rank):
     for T in ([args.topk] if args.topk else cfg["sweep"]):
         ids, _, st = ix.search(q_std, mode=args.mode, K=K, topk_size=T)
         torch.cuda.synchronize()
+        if st.error_flags:
+            raise SystemExit(f"search kernel reported error flags {st.error_flags:#x}")
         r = recall_at_k(ids.cpu().numpy().astype(np.int64), gt)
         sweep.append({"topk_size": T, "recall@10": round(r, 5)})
         if r >= TARGET_RECALL:
@@ -280,14 +328,17 @@ def run_ours(args, rank, world, local_rank):
 
     # per-query counters at the operating point (untimed) for the roofline
     q_dev = torch.from_numpy(queries).to(dev)
-    ids_d = torch.empty((NQ_PER_GPU, K), dtype=torch.int32, device=dev)
-    dists_d = torch.empty((NQ_PER_GPU, K), dtype=torch.float32, device=dev)
+    ids_d = torch.empty((nq, K), dtype=torch.int32, device=dev)
+    dists_d = torch.empty((nq, K), dtype=torch.float32, device=dev)
     _, _, st = ix.search(q_dev, params)
     torch.cuda.synchronize()
+    if st.error_flags:
+        raise SystemExit(f"search kernel reported error flags {st.error_flags:#x}")
     dim, deg = base.shape[1], edges.shape[1]
     # query read + per expansion either one neighbourhood block (adjacency row
     # and all neighbour rows, copied whole) or the adjacency row and the rows of
     # the scored candidates as stored (u8 copy: 1 B/dim) + ids and distances
+    useful_d = None
     if args.mode == "rabitq":
         # per expansion: adjacency row, the neighbours' 1-bit codes (pdim/8 B
         # each) and 3 f32 factors each, and the parent's exact row; then the
@@ -295,17 +346,25 @@ def run_ours(args, rank, world, local_rank):
         pdim = 1 << (dim - 1).bit_length()
         per_expansion = (st.expansions * (4 * deg + deg * pdim // 8 + 12 * deg + st.row_bytes)
                          + st.rerank * st.row_bytes)
+        useful = per_expansion
     elif st.block_bytes:
         per_expansion = st.expansions * st.block_bytes
+        # the bytes the search needs in the stored row format: adjacency rows
+        # and the rows of the distinct candidates the reference scores
+        useful_d, _ = useful_distance_count(B, base, edges, queries, params, local_rank)
+        useful = st.expansions * 4 * deg + useful_d * st.row_bytes
     else:
         per_expansion = st.expansions * 4 * deg + st.distances * st.row_bytes
-    alg_bytes = NQ_PER_GPU * 4 * dim + per_expansion + NQ_PER_GPU * 8 * K
+        useful = per_expansion
+    io_bytes = nq * 4 * dim + nq * 8 * K
+    alg_bytes = io_bytes + per_expansion
+    useful_bytes = io_bytes + useful
 
     stream = torch.cuda.Stream(device=dev)
     flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
 
     def step():
-        ix.search_raw(q_dev.data_ptr(), NQ_PER_GPU, ids_d.data_ptr(), dists_d.data_ptr(), params,
+        ix.search_raw(q_dev.data_ptr(), nq, ids_d.data_ptr(), dists_d.data_ptr(), params,
                       stream=stream.cuda_stream)
 
     with torch.cuda.stream(stream):
@@ -330,45 +389,52 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize()
     step_ms = [a.elapsed_time(b) for a, b in ev]
     t_ms = sum(step_ms)
+    # the timed launches are asynchronous: their kernels' error bits are in the
+    # index's error word
+    kernel_errors = ix.take_errors(stream.cuda_stream)
 
     # e2e through the same public call with pinned host buffers
     hq = torch.from_numpy(queries).pin_memory()
-    hid = torch.empty((NQ_PER_GPU, K), dtype=torch.int32).pin_memory()
-    hdist = torch.empty((NQ_PER_GPU, K), dtype=torch.float32).pin_memory()
+    hid = torch.empty((nq, K), dtype=torch.int32).pin_memory()
+    hdist = torch.empty((nq, K), dtype=torch.float32).pin_memory()
     e2e_steps = max(3, min(args.steps, 10))
     for _ in range(2):
-        ix.search_raw(hq.data_ptr(), NQ_PER_GPU, hid.data_ptr(), hdist.data_ptr(), params, stream=stream.cuda_stream)
+        ix.search_raw(hq.data_ptr(), nq, hid.data_ptr(), hdist.data_ptr(), params, stream=stream.cuda_stream)
     ee = []
     for _ in range(e2e_steps):
         with torch.cuda.stream(stream):
             flush.zero_()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(stream)
-        ix.search_raw(hq.data_ptr(), NQ_PER_GPU, hid.data_ptr(), hdist.data_ptr(), params, stream=stream.cuda_stream)
+        ix.search_raw(hq.data_ptr(), nq, hid.data_ptr(), hdist.data_ptr(), params, stream=stream.cuda_stream)
         b.record(stream)
         b.synchronize()
         ee.append(a.elapsed_time(b))
     e2e_ms = statistics.mean(ee)
     assert np.array_equal(hid.numpy(), ids_d.cpu().numpy()), "e2e results differ from device-resident results"
+    kernel_errors |= ix.take_errors(stream.cuda_stream)
 
-    # max over ranks
+    # max over ranks (and any rank's kernel error bits)
     if world > 1:
-        t = torch.tensor([t_ms, e2e_ms], dtype=torch.float64, device=dev)
+        t = torch.tensor([t_ms, e2e_ms, float(kernel_errors)], dtype=torch.float64, device=dev)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        t_ms, e2e_ms = float(t[0]), float(t[1])
+        t_ms, e2e_ms, kernel_errors = float(t[0]), float(t[1]), int(t[2])
+    if kernel_errors:
+        raise SystemExit(f"search kernels reported error flags {kernel_errors:#x} during the timed run")
     ms_per_step = t_ms / args.steps
-    value = world * NQ_PER_GPU / (ms_per_step / 1e3)
-    e2e_value = world * NQ_PER_GPU / (e2e_ms / 1e3)
+    value = nq_job / (ms_per_step / 1e3)
+    e2e_value = nq_job / (e2e_ms / 1e3)
 
     if rank != 0:
         return None
     peak, peak_kind = peaks()
     achieved = alg_bytes / (statistics.mean(step_ms) / 1e3) / 1e9
+    achieved_useful = useful_bytes / (statistics.mean(step_ms) / 1e3) / 1e9
     traffic = None
     # DRAM bytes of one launch of this kernel on this workload, from the ncu
     # capture summarised in profiles/k_search_nb_c2.md
     tp = os.path.join(ROOT, "profiles", f"traffic_{CFG_NAME}.json")
-    if os.path.exists(tp):
+    if os.path.exists(tp) and not strong and world == 1:
         with open(tp) as f:
             tj = json.load(f)
         if tj.get("topk_size") == chosen and tj.get("mode") == args.mode and tj.get("layout") == (
@@ -383,27 +449,31 @@ def run_ours(args, rank, world, local_rank):
         "warmup": args.warmup,
         "ms_per_step": round(ms_per_step, 4),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if strong else "weak",
         "vs_baseline": None,
         # rows stored as bytes (128 B for the 128-d C2 rows): u8 products
         # summed exactly in int32 with __dp4a
         "dtype": "u8" if st.integer_exact and st.row_bytes == base.shape[1] else "f32",
         "data": cfg["data"],
         "config": {
-            "workload": cfg["workload"],
+            "workload": cfg["workload"] if not strong else cfg["workload"].replace(
+                "per GPU", f"split over {world} GPU(s)"),
             "mode": args.mode, "K": K, "topk_size": chosen,
             "recall@10": sweep[-1]["recall@10"] if chosen == sweep[-1]["topk_size"] else None,
             "recall_sweep": sweep,
             "entry_point": entry,
+            "queries_per_gpu": nq,
             "distance_path": ("integer-exact" if st.integer_exact else "sequential per lane")
                              + f", stored row {st.row_bytes} B",
             "layout": (f"neighbourhood blocks, {st.block_bytes} B bulk copy per expansion"
                        if st.block_bytes else "gather"),
-            "expansions_per_query": round(st.expansions / NQ_PER_GPU, 2),
-            "distances_per_query": round(st.distances / NQ_PER_GPU, 2),
+            "expansions_per_query": round(st.expansions / nq, 2),
+            "distances_per_query": round(st.distances / nq, 2),
+            "reference_distances_per_query": round(useful_d / nq, 2) if useful_d is not None else None,
             "l2": "256 MiB write before every timed step (outside the timed window); index "
                   f"{(base.nbytes * (st.row_bytes / (4 * base.shape[1])) + edges.nbytes) / 1e6:.0f} MB > L2",
             "parallelism": f"query-sharded dp{world}, replicated index",
+            "kernel_errors": kernel_errors,
         },
         "roofline": {
             "bound": "hbm",
@@ -414,16 +484,54 @@ def run_ours(args, rank, world, local_rank):
             "traffic": traffic,
             "peak_kind": peak_kind,
             "algorithmic_bytes_per_launch": int(alg_bytes),
+            # the same time over the bytes the search itself needs (adjacency
+            # rows + the rows of the distinct candidates the reference scores,
+            # as stored): the layout moves more than that to save a round trip
+            "useful_bytes_per_launch": int(useful_bytes),
+            "achieved_useful": round(achieved_useful, 1),
+            "frac_useful": round(achieved_useful / peak, 4),
         },
         "e2e": {"value": round(e2e_value, 1), "unit": "queries/s",
-                "h2d_bytes_per_step": int(NQ_PER_GPU * base.shape[1] * 4),
-                "d2h_bytes_per_step": int(NQ_PER_GPU * K * 8)},
+                "h2d_bytes_per_step": int(nq * base.shape[1] * 4),
+                "d2h_bytes_per_step": int(nq * K * 8)},
         "gpu_launches": args.steps,
         "clocks": clk.summary(),
     }
-    if not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(base, queries, chosen, entry, codebook, sample=args.cpu_sample)
+    if not args.no_cpu_baseline and world == 1:
+        line["cpu_baseline"], ref_ids = cpu_baseline(base, queries, chosen, entry, codebook, sample=args.cpu_sample)
+        if ref_ids is not None:
+            line["parity"] = parity_vs_reference(ref_ids, ids_d.cpu().numpy().view(np.uint32),
+                                                 dists_d.cpu().numpy(), base, queries, gt)
     return line
+
+
+def parity_vs_reference(ref_ids, ids, dists, base, queries, gt):
+    """Our result rows against the reference CPU search's rows for the same
+    queries (the first len(ref_ids) of this rank's): identical rows, ids in
+    agreement, our distances against the exact distances of the reference's
+    ids (float64), and recall@10 of both against the exact top-10."""
+    n = ref_ids.shape[0]
+    ours = ids[:n]
+    same_rows = (ours == ref_ids).all(axis=1)
+    agree = (ours == ref_ids)
+    sel = ref_ids != 0xFFFFFFFF
+    q = queries[:n].astype(np.float64)
+    rel = 0.0
+    for i in range(n):
+        m = agree[i] & sel[i]
+        if not m.any():
+            continue
+        x = base[ref_ids[i][m]].astype(np.float64)
+        exact = ((x - q[i]) ** 2).sum(axis=1)
+        rel = max(rel, float(np.max(np.abs(dists[i][m] - exact) / np.maximum(exact, 1e-30))))
+    r_ours = recall_at_k(ours.astype(np.int64), gt[:n])
+    r_ref = recall_at_k(ref_ids.astype(np.int64), gt[:n])
+    return {"queries": int(n), "identical_rows": round(float(same_rows.mean()), 6),
+            "ids_match_frac": round(float(agree.mean()), 6), "max_rel_dist_err": rel,
+            "recall@10_ours": round(r_ours, 5), "recall@10_reference": round(r_ref, 5),
+            "recall_delta": round(r_ours - r_ref, 5),
+            "against": "the reference's own CPU search (oracle/_ref/ref_search_omp) on the same graph, "
+                       "queries, entry point, K and topk_size"}
 
 
 # ------------------------------------------------------ reference CPU arm
@@ -436,14 +544,15 @@ def _write_inputs(tmp, base, queries):
     return os.path.join(DATA_DIR, CFG_NAME, "graph.bin"), bp, qp
 
 
-def _ref_search(paths, topk, entry, nq, codebook=None, threads=None):
+def _ref_search(paths, topk, entry, nq, codebook=None, out=None):
+    """The reference CPU search on all host threads (explicitly: torchrun's
+    OMP_NUM_THREADS=1 must not reach it).  Returns (info, ids or None)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
     g, b, q = paths
     mode = "rabitq" if codebook else "base"
-    info, _ = O.run_ref_search(g, b, q, K=K, topk=topk, mode=mode, codebook=codebook, threads=threads, nq=nq,
-                               entry=entry)
-    return info
+    return O.run_ref_search(g, b, q, K=K, topk=topk, mode=mode, codebook=codebook, threads=host_threads(), nq=nq,
+                            entry=entry, out=out)
 
 
 def _ref_class(codebook):
@@ -452,17 +561,21 @@ def _ref_class(codebook):
 
 
 def cpu_baseline(base, queries, topk, entry, codebook=None, sample=2000):
+    """The reference CPU search timed on a bounded sample of this workload's
+    queries; also returns its result ids for the parity check (None when the
+    reference tools were not built)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
     if O.ref_tool("ref_search_omp") is None:
         return {"value": None, "unit": "queries/s", "cores": 0, "kind": "reference",
-                "sample": "unavailable: oracle/_ref/ref_search_omp not built"}
+                "sample": "unavailable: oracle/_ref/ref_search_omp not built"}, None
     with tempfile.TemporaryDirectory() as tmp:
         paths = _write_inputs(tmp, base, queries)
-        info = _ref_search(paths, topk, entry, min(sample, len(queries)), codebook)
+        info, ids = _ref_search(paths, topk, entry, min(sample, len(queries)), codebook,
+                                out=os.path.join(tmp, "ref_ids.u32"))
     return {"value": round(info["qps"], 1), "unit": "queries/s", "cores": info["threads"], "kind": "reference",
             "sample": f"first {info['nq']} of the {len(queries)} queries, {_ref_class(codebook)} "
-                      f"under OpenMP on all host threads, topk_size {topk}, K {K}"}
+                      f"under OpenMP on {info['threads']} host threads, topk_size {topk}, K {K}"}, ids
 
 
 def run_reference(args, rank, world):
@@ -485,7 +598,7 @@ def run_reference(args, rank, world):
         paths = _write_inputs(tmp, base, queries_all)
         for _ in range(args.warmup):
             _ref_search(paths, topk, entry, sample, codebook)
-        infos = [_ref_search(paths, topk, entry, sample, codebook) for _ in range(args.steps)]
+        infos = [_ref_search(paths, topk, entry, sample, codebook)[0] for _ in range(args.steps)]
     secs = sum(i["seconds"] for i in infos)
     nq = sum(i["nq"] for i in infos)
     value = nq / secs
@@ -500,7 +613,7 @@ def run_reference(args, rank, world):
         "warmup": args.warmup,
         "ms_per_step": round(1e3 * secs / args.steps, 3),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": args.scaling,
         "vs_baseline": None,
         "dtype": "f32",
         "data": cfg["data"],
@@ -626,6 +739,9 @@ def main():
     ap.add_argument("--cpu-sample", type=int, default=2000)
     ap.add_argument("--ref-sample", type=int, default=1000)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--scaling", choices=("weak", "strong"), default="weak",
+                    help="weak: every GPU searches its own 10,000 queries; strong: the workload's 10,000 "
+                         "queries split over the GPUs")
     ap.add_argument("--measure", choices=("search", "codebook"), default="search",
                     help="codebook: time the GPU codebook builder instead of the search")
     ap.add_argument("--profile-run", action="store_true",

@@ -6,8 +6,7 @@
  * gpu_cli main() builds device copies of the graph and codebook and calls
  * templated launchers directly.  Each entry point below names the reference
  * piece it replaces (reference-relative file:line), so a host program written
- * against the reference structure can bind this library one to one (see
- * INTEGRATION.md for the binding a maintainer would add).
+ * against the reference structure can bind this library one to one.
  *
  * Threading: an index is bound to one CUDA device.  bs_search may run
  * concurrently on different streams; each call uses its own scratch.
@@ -133,6 +132,17 @@ BS_API bs_status bs_index_entry_point(bs_index* index, uint32_t* entry);
  * codebook is attached (reference src/gpu_cli.cu:436-437). */
 BS_API bs_status bs_index_rabitq_entry(const bs_index* index, uint32_t* entry);
 
+/* No counterpart in the reference, whose kernels have no error channel.
+ * Every search kernel on this index also ORs its error bits (the ones
+ * bs_search reports as BS_ERR_KERNEL) into a word held by the index, so that a
+ * caller of asynchronous searches -- bs_search with device buffers and no
+ * stats, or bs_search_no_alloc -- can collect them later: this call copies
+ * the word to *flags and clears it, ordered after the work already queued on
+ * `stream`, and synchronises `stream`.  Bits: 1 a visited-table probe ran the
+ * whole table, 2 a RaBitQ visited table overflowed, 4 a block copy's wait
+ * gave up, 8 that copy never landed.  0 means no kernel reported an error. */
+BS_API bs_status bs_index_take_errors(bs_index* index, void* stream, uint32_t* flags);
+
 BS_API void bs_index_destroy(bs_index* index);
 
 /* Replaces run_base / run_warp / run_rabitq and their kernels
@@ -171,7 +181,8 @@ BS_API bs_status bs_search(bs_index* index, const bs_search_params* params, cons
  *   - all calls share the one array, which keeps the last call's contents
  *     (the counters are cleared at the start of every call): calls that
  *     overlap on the GPU race, so serialise them (one stream, or events);
- *   - asynchronous on `stream`; no statistics are returned. */
+ *   - asynchronous on `stream`; no statistics are returned (kernel error
+ *     bits reach the index's error word: bs_index_take_errors). */
 BS_API bs_status bs_search_no_alloc(bs_index* index, const bs_search_params* params, const float* queries,
                                     uint32_t nq, uint32_t* ids, float* dists, void* stream);
 

@@ -1,5 +1,5 @@
 """Regenerates the golden fixtures under tests/golden/ from the reference's own
-tools (compiled into oracle/_ref/ by `make -C oracle`):
+tools (compiled into oracle/_ref/ by `make -C oracle REF=<reference tree>`):
 
 * base / query vectors: the seeded generators of beam_search_collab_b200.datasets
   (not stored; regenerated bit-identically by the tests)
@@ -97,7 +97,7 @@ def make_set(name, gen, kw, degree, with_cb, runs, tmp):
 
 def main():
     if O.ref_tool("build_graph") is None:
-        raise SystemExit("oracle/_ref tools missing: run `make -C oracle` where the reference tree exists")
+        raise SystemExit("oracle/_ref tools missing: run `make -C oracle REF=<reference tree>`")
     with tempfile.TemporaryDirectory() as tmp:
         for name, (gen, kw, degree, with_cb, runs) in SETS.items():
             make_set(name, gen, kw, degree, with_cb, runs, tmp)

@@ -46,6 +46,10 @@ def test_no_alloc_matches_bs_search_on_two_calls(name, mode, K, topk):
             assert rc == 0, B.lib().bs_last_error().decode()
             torch.cuda.synchronize()
             outs.append((ids, dists))
+            # the first call computed the entry point in the fixed array: it
+            # must be the reference's (cpu_cli's printed entry)
+            assert ix.entry_point() == g.entry
+        assert ix.take_errors() == 0                  # no kernel error bits
         ref_ids, ref_d, st = ix.search(q, params)     # the regular entry point
         torch.cuda.synchronize()
         assert st.error_flags == 0
