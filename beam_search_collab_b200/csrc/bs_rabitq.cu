@@ -357,9 +357,7 @@ cudaError_t rabitq_grid(const SearchParams& p, const LaunchShape& shape, int num
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, smem);
     if (e != cudaSuccess) return e;
     if (per_sm < 1) return cudaErrorInvalidConfiguration;
-    const uint64_t want = (static_cast<uint64_t>(p.nq) + shape.warps_per_block - 1) / shape.warps_per_block;
-    const uint64_t cap = static_cast<uint64_t>(per_sm) * static_cast<uint64_t>(num_sms);
-    grid = static_cast<unsigned>(want < cap ? want : cap);
+    grid = persistent_blocks(p.nq, shape.warps_per_block, per_sm, num_sms);
     return cudaSuccess;
 }
 

@@ -492,9 +492,7 @@ cudaError_t launch_search_nb(const SearchParams& p, const LaunchShape& shape, in
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, smem);
     if (e != cudaSuccess) return e;
     if (per_sm < 1) return cudaErrorInvalidConfiguration;
-    const uint64_t want = (static_cast<uint64_t>(p.nq) + shape.warps_per_block - 1) / shape.warps_per_block;
-    const uint64_t cap = static_cast<uint64_t>(per_sm) * static_cast<uint64_t>(num_sms);
-    const unsigned grid = static_cast<unsigned>(want < cap ? want : cap);
+    const unsigned grid = persistent_blocks(p.nq, shape.warps_per_block, per_sm, num_sms);
     if (grid == 0) return cudaSuccess;
     fn<<<grid, threads, smem, stream>>>(p);
     return cudaGetLastError();

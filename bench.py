@@ -275,7 +275,11 @@ def useful_distance_count(B, base, edges, queries, params, local_rank):
         else:
             os.environ["BSEARCH_LAYOUT"] = old
     try:
-        p = B.SearchParams(mode=params.mode, K=params.K, topk_size=params.topk_size, filter_capacity=1 << 15)
+        # one warp per block: room for a 16k-slot table (reset only past 12k
+        # inserts, i.e. hundreds of expansions); the results do not depend on
+        # the warps per block
+        mode = "warp1" if params.mode in ("base", "warp1", "warp2", "warp4", "warp8") else params.mode
+        p = B.SearchParams(mode=mode, K=params.K, topk_size=params.topk_size, filter_capacity=1 << 14)
         _, _, st = gx.search(queries, p, with_dists=False)
         return st.distances, st.expansions
     finally:
