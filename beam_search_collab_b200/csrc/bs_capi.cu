@@ -60,6 +60,18 @@ struct bs_index {
     uint32_t* d_codes = nullptr;
     float* d_factors = nullptr;
     float* d_signs = nullptr;
+    // RaBitQ node blocks [adjacency | codes | factors | own row], one bulk
+    // copy per expansion (null: the gather kernel)
+    unsigned char* d_rqb = nullptr;
+    uint32_t rq_stride = 0, rq_off_codes = 0, rq_off_fac = 0, rq_off_row = 0;
+    // RaBitQ visited arena (per resident warp: bitmap + log), kept between
+    // calls and all zero between queries; rabitq calls on this index are
+    // ordered one after another through rq_event
+    std::mutex rq_mu;
+    uint32_t* d_vis = nullptr;
+    uint64_t vis_warps = 0;
+    uint32_t vis_words = 0, vis_log_cap = 0;
+    cudaEvent_t rq_event = nullptr;
     // error word every search kernel on this index ORs its error bits into
     // (read and cleared by bs_index_take_errors)
     unsigned int* d_err = nullptr;
@@ -296,9 +308,106 @@ cudaError_t build_blocks(bs_index* ix) {
     return e;
 }
 
+// RaBitQ node blocks [adjacency | codes | factors | own row] (16-byte aligned
+// parts), built on the GPU from the attached codebook when they take at most
+// 40% of the free memory; BSEARCH_LAYOUT=gather keeps the gather kernel.
+cudaError_t build_rq_blocks(bs_index* ix) {
+    cudaFree(ix->d_rqb);
+    ix->d_rqb = nullptr;
+    const char* env = std::getenv("BSEARCH_LAYOUT");
+    if (env && std::strcmp(env, "gather") == 0) return cudaSuccess;
+    if (ix->degree > 64) return cudaSuccess;
+    auto a16 = [](uint64_t x) { return (x + 15u) & ~static_cast<uint64_t>(15u); };
+    const uint64_t deg = static_cast<uint64_t>(ix->degree), wpp = static_cast<uint64_t>(ix->pdim) / 32u;
+    const uint64_t off_codes = a16(4u * deg);
+    const uint64_t off_fac = a16(off_codes + 4u * deg * wpp);
+    const uint64_t off_row = a16(off_fac + 12u * deg);
+    const uint64_t stride = a16(off_row + (ix->u8 ? ix->row_bytes : ix->row_stride * 4u));
+    if (stride > 48u * 1024u) return cudaSuccess;
+    size_t free_b = 0, total_b = 0;
+    if (cudaMemGetInfo(&free_b, &total_b) != cudaSuccess) { cudaGetLastError(); return cudaSuccess; }
+    const uint64_t bytes = stride * ix->n;
+    if (bytes > free_b / 5u * 2u) return cudaSuccess;
+    if (cudaMalloc(&ix->d_rqb, bytes) != cudaSuccess) {
+        cudaGetLastError();
+        ix->d_rqb = nullptr;
+        return cudaSuccess;
+    }
+    ix->rq_stride = static_cast<uint32_t>(stride);
+    ix->rq_off_codes = static_cast<uint32_t>(off_codes);
+    ix->rq_off_fac = static_cast<uint32_t>(off_fac);
+    ix->rq_off_row = static_cast<uint32_t>(off_row);
+    SearchParams p{};
+    p.vecs = ix->d_vecs;
+    p.vecs8 = ix->d_vecs8;
+    p.row_bytes = ix->row_bytes;
+    p.row_stride = ix->row_stride;
+    p.adj = ix->d_adj;
+    p.n = ix->n;
+    p.degree = static_cast<uint32_t>(ix->degree);
+    p.codes = ix->d_codes;
+    p.factors = ix->d_factors;
+    p.wpp = static_cast<uint32_t>(wpp);
+    p.rq_stride = ix->rq_stride;
+    p.rq_off_codes = ix->rq_off_codes;
+    p.rq_off_fac = ix->rq_off_fac;
+    p.rq_off_row = ix->rq_off_row;
+    cudaError_t e = bsb::build_rabitq_blocks(p, ix->d_rqb, nullptr);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    return e;
+}
+
+// The RaBitQ visited arena for `warps` resident warps: one bitmap over the
+// node ids and one log per warp, zeroed once.  Shrinks the warps to fit a
+// quarter of the free memory.  Called with ix->rq_mu held.
+bs_status ensure_visited_arena(bs_index* ix, uint64_t warps, uint32_t warps_per_block) {
+    const uint32_t words = static_cast<uint32_t>(((ix->n + 31u) / 32u + 3u) & ~3ull);
+    // ids one query may log before its end clears the whole bitmap instead;
+    // BSEARCH_RQ_LOG_CAP overrides it (tests reach the whole-bitmap path)
+    uint32_t kLogCap = 16384;
+    if (const char* c = std::getenv("BSEARCH_RQ_LOG_CAP")) kLogCap = static_cast<uint32_t>(std::strtoul(c, nullptr, 10));
+    kLogCap = (kLogCap + 3u) & ~3u;
+    if (ix->d_vis && ix->vis_warps >= warps && ix->vis_words == words) return BS_OK;
+    cudaError_t e;
+    if (!ix->rq_event && (e = cudaEventCreateWithFlags(&ix->rq_event, cudaEventDisableTiming)) != cudaSuccess)
+        return cuda_fail(e, "rabitq event");
+    if (ix->d_vis) {
+        // the previous arena may still be in use by a queued search
+        if ((e = cudaEventSynchronize(ix->rq_event)) != cudaSuccess) return cuda_fail(e, "rabitq arena");
+        cudaFree(ix->d_vis);
+        ix->d_vis = nullptr;
+        ix->vis_warps = 0;
+    }
+    const uint64_t per_warp = (static_cast<uint64_t>(words) + kLogCap) * 4u;
+    size_t free_b = 0, total_b = 0;
+    if ((e = cudaMemGetInfo(&free_b, &total_b)) != cudaSuccess) return cuda_fail(e, "cudaMemGetInfo");
+    uint64_t fit = (free_b / 4u) / per_warp;
+    fit -= fit % warps_per_block;
+    if (warps > fit) warps = fit;
+    if (warps < warps_per_block)
+        return fail(BS_ERR_OUT_OF_MEMORY, "RaBitQ visited arena: %llu bytes per warp do not fit",
+                    static_cast<unsigned long long>(per_warp));
+    if ((e = cudaMalloc(&ix->d_vis, warps * per_warp)) != cudaSuccess) return cuda_fail(e, "rabitq visited arena");
+    if ((e = cudaMemset(ix->d_vis, 0, warps * per_warp)) != cudaSuccess) return cuda_fail(e, "rabitq visited arena");
+    ix->vis_warps = warps;
+    ix->vis_words = words;
+    ix->vis_log_cap = kLogCap;
+    return BS_OK;
+}
+
 // Plans the launch; when a neighbourhood block per warp does not fit the
 // requested warps per block in shared memory, plans the gather layout.
 cudaError_t plan(const bs_index* ix, SearchParams& p, LaunchShape& shape, char* why, size_t why_len) {
+    if (p.rq_nb) {
+        SearchParams p1 = p;
+        LaunchShape s1 = shape;
+        if (bsb::plan_search_rq_nb(p1, s1, ix->smem_optin, why, why_len) == cudaSuccess) {
+            p = p1;
+            shape = s1;
+            return cudaSuccess;
+        }
+        p.rq_nb = nullptr;   // the gather kernel
+    }
     SearchParams p0 = p;
     const LaunchShape s0 = shape;
     const cudaError_t e = bsb::plan_search(p, shape, ix->smem_optin, why, why_len);
@@ -340,6 +449,16 @@ void fill_params(const bs_index* ix, const ModeInfo& mi, const bs_search_params*
         p.signs = ix->d_signs;
         p.pdim = static_cast<uint32_t>(ix->pdim);
         p.wpp = static_cast<uint32_t>(ix->pdim) / 32u;
+        if (ix->d_rqb) {
+            p.rq_nb = ix->d_rqb;
+            p.rq_stride = ix->rq_stride;
+            p.rq_off_codes = ix->rq_off_codes;
+            p.rq_off_fac = ix->rq_off_fac;
+            p.rq_off_row = ix->rq_off_row;
+            // BSEARCH_RQ_ESTIMATOR=lut: the nibble-table estimator (same sums)
+            const char* est = std::getenv("BSEARCH_RQ_ESTIMATOR");
+            p.rq_lut = (est && std::strcmp(est, "lut") == 0) ? 1u : 0u;
+        }
     }
     p.topk = prm->topk_size;
     p.K = static_cast<uint32_t>(prm->K);
@@ -374,6 +493,9 @@ void free_index(bs_index* ix) {
     cudaFree(ix->d_factors);
     cudaFree(ix->d_signs);
     cudaFree(ix->d_err);
+    cudaFree(ix->d_rqb);
+    cudaFree(ix->d_vis);
+    if (ix->rq_event) cudaEventDestroy(ix->rq_event);
     delete ix;
 }
 
@@ -549,6 +671,7 @@ BS_API bs_status bs_index_attach_rabitq(bs_index* ix, const bs_rabitq_desc* d) {
     ix->pdim = pdim;
     ix->rq_entry = d->entry_point;
     ix->has_rabitq = true;
+    if ((e = build_rq_blocks(ix)) != cudaSuccess) return cuda_fail(e, "rabitq node blocks");
     return BS_OK;
 }
 
@@ -682,6 +805,7 @@ BS_API bs_status bs_index_build_codebook(bs_index* ix, uint32_t seed, const char
     ix->rq_entry = entry;
     ix->has_rabitq = true;
     if (entry_out) *entry_out = entry;
+    if ((e = build_rq_blocks(ix)) != cudaSuccess) return cuda_fail(e, "rabitq node blocks");
     return BS_OK;
 }
 
@@ -765,7 +889,7 @@ BS_API bs_status bs_search(bs_index* ix, const bs_search_params* prm, const floa
         stats->entry_point = entry;
         stats->integer_exact = use_team ? 1u : 0u;
         stats->row_bytes = ix->u8 ? ix->row_bytes : ix->row_stride * 4u;
-        stats->block_bytes = p.nb ? p.nb_stride : 0u;
+        stats->block_bytes = p.nb ? p.nb_stride : p.rq_nb ? p.rq_stride : 0u;
     }
     if (nq == 0) return BS_OK;
 
@@ -795,7 +919,7 @@ BS_API bs_status bs_search(bs_index* ix, const bs_search_params* prm, const floa
     const size_t d_off = off;
     if (d_stage) off += (obytes + 255) & ~static_cast<size_t>(255);
     const size_t s_off = off;
-    if (mi.rabitq) {
+    if (mi.rabitq && !p.rq_nb) {
         uint64_t warps = 0;
         e0 = bsb::rabitq_grid_warps(p, shape, ix->num_sms, warps);
         if (e0 != cudaSuccess) return cuda_fail(e0, "rabitq launch shape");
@@ -811,16 +935,34 @@ BS_API bs_status bs_search(bs_index* ix, const bs_search_params* prm, const floa
     p.queries_src = q_map;
     p.out_ids = i_dev ? ids : i_map ? i_map : reinterpret_cast<uint32_t*>(scratch + i_off);
     p.out_dists = !dists ? nullptr : d_dev ? dists : d_map ? d_map : reinterpret_cast<float*>(scratch + d_off);
-    p.spill = mi.rabitq ? reinterpret_cast<uint32_t*>(scratch + s_off) : nullptr;
+    p.spill = (mi.rabitq && !p.rq_nb) ? reinterpret_cast<uint32_t*>(scratch + s_off) : nullptr;
 
     e = cudaMemsetAsync(scratch, 0, sizeof(DevCounters), stream);
     if (e == cudaSuccess && !q_dev && !q_map)
         e = cudaMemcpyAsync(scratch + q_off, queries, qbytes, cudaMemcpyHostToDevice, stream);
     if (e != cudaSuccess) { release(); return cuda_fail(e, "query upload"); }
 
-    e = mi.rabitq ? bsb::launch_search_rabitq(p, shape, ix->num_sms, stream)
-        : p.nb    ? bsb::launch_search_nb(p, shape, ix->num_sms, stream)
-                  : bsb::launch_search(p, shape, ix->num_sms, stream);
+    if (p.rq_nb) {
+        // RaBitQ over node blocks: the index's visited arena, used by one
+        // call at a time (stream order through rq_event)
+        std::lock_guard<std::mutex> lk(ix->rq_mu);
+        uint64_t cap = 0;
+        e = bsb::rq_nb_capacity_warps(p, shape, ix->num_sms, cap);
+        if (e != cudaSuccess) { release(); return cuda_fail(e, "rabitq launch shape"); }
+        const bs_status as = ensure_visited_arena(ix, cap, static_cast<uint32_t>(shape.warps_per_block));
+        if (as != BS_OK) { release(); return as; }
+        p.vis = ix->d_vis;
+        p.vis_words = ix->vis_words;
+        p.vis_log_cap = ix->vis_log_cap;
+        p.vis_warps = static_cast<uint32_t>(ix->vis_warps);
+        e = cudaStreamWaitEvent(stream, ix->rq_event, 0);
+        if (e == cudaSuccess) e = bsb::launch_search_rq_nb(p, shape, ix->num_sms, stream);
+        if (e == cudaSuccess) e = cudaEventRecord(ix->rq_event, stream);
+    } else {
+        e = mi.rabitq ? bsb::launch_search_rabitq(p, shape, ix->num_sms, stream)
+            : p.nb    ? bsb::launch_search_nb(p, shape, ix->num_sms, stream)
+                      : bsb::launch_search(p, shape, ix->num_sms, stream);
+    }
     if (e != cudaSuccess) { release(); return cuda_fail(e, "search launch"); }
 
     if (i_stage) e = cudaMemcpyAsync(ids, scratch + i_off, obytes, cudaMemcpyDeviceToHost, stream);

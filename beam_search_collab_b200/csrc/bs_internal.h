@@ -132,6 +132,23 @@ struct SearchParams {
     // a caller of an asynchronous search can collect them later
     unsigned int* sticky_err;
     uint32_t wait_polls;        // first bounded wait of an expansion (polls)
+    // RaBitQ node blocks (null: the gather kernel): per node, its adjacency
+    // row (repeats -> 0xffffffff), its neighbours' codes [degree][wpp], its
+    // factors [3][degree] and its own row as stored, rq_stride bytes per node
+    const unsigned char* rq_nb;
+    uint32_t rq_stride;
+    uint32_t rq_off_codes;
+    uint32_t rq_off_fac;
+    uint32_t rq_off_row;
+    uint32_t rq_lut;            // 1: estimator through a per-query nibble table
+    uint32_t off_est;           // per-warp bit-planes or nibble table
+    // RaBitQ visited sets: per resident warp, a bitmap of vis_words words over
+    // the node ids, then a log of vis_log_cap ids set by the current query
+    // (cleared word by word when the query ends); all zero between queries
+    uint32_t* vis;
+    uint32_t vis_words;
+    uint32_t vis_log_cap;
+    uint32_t vis_warps;         // warps the visited arena holds (grid cap)
 };
 
 #ifdef __CUDACC__
@@ -187,6 +204,15 @@ cudaError_t launch_search_nb(const SearchParams& p, const LaunchShape& shape, in
                              cudaStream_t stream);
 // Builds the neighbourhood blocks from the gather layout (bs_search_nb.cu).
 cudaError_t build_neighbourhood_blocks(const SearchParams& p, unsigned char* out, cudaStream_t stream);
+
+// RaBitQ over node blocks (bs_rabitq_nb.cu): plan (shared-memory carve-up),
+// resident warps of the planned launch (sizes the visited arena), launch, and
+// the block builder (from the gather layout: adj, codes, factors, rows).
+cudaError_t plan_search_rq_nb(SearchParams& p, LaunchShape& shape, size_t max_smem_optin, char* why,
+                              size_t why_len);
+cudaError_t rq_nb_capacity_warps(const SearchParams& p, const LaunchShape& shape, int num_sms, uint64_t& warps);
+cudaError_t launch_search_rq_nb(const SearchParams& p, const LaunchShape& shape, int num_sms, cudaStream_t stream);
+cudaError_t build_rabitq_blocks(const SearchParams& p, unsigned char* out, cudaStream_t stream);
 
 // Resident warps of the RaBitQ launch for `shape` (sizes the spill tables).
 cudaError_t rabitq_grid_warps(const SearchParams& p, const LaunchShape& shape, int num_sms,

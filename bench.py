@@ -84,6 +84,15 @@ CONFIGS = {
                         "(build_rabitq seed 12345), K=10, exact rerank",
                data="synthetic: seeded C3 mixture (256 clusters on the unit sphere, concentration 20), graph "
                     "and codebook from the reference build_graph / build_rabitq"),
+    # C2 with a RaBitQ codebook (dim 128 = padded_dim, so the codes cover every
+    # rotated component; the reference build_rabitq, seed 12345, makes it on
+    # first use): a RaBitQ workload with a real recall/QPS curve
+    "c2rq": dict(gen="gen_c2", nq=10_000, mode="rabitq", K=10, sweep=(32, 48, 64, 96, 128, 192, 256, 384, 512),
+                 codebook=True, data_dir="c2",
+                 workload="C2 + RaBitQ: 1M x 128 int-valued base, 10k queries per GPU, degree-32 Vamana, "
+                          "RaBitQ codebook (build_rabitq seed 12345), K=10, exact rerank",
+                 data="synthetic: seeded C2 mixture (1,024 Gaussians, ints 0..255), graph and codebook from the "
+                      "reference build_graph / build_rabitq"),
     "c4": dict(gen="gen_c4", nq=1_000, mode="base", K=100, sweep=(256,), codebook=False,
                workload="C4: 1M x 960 non-negative base, 1k queries per GPU, degree-32 Vamana, K=100, topk 256",
                data="synthetic: seeded C4 (|N(0,1)| * 0.1 * per-dimension log-uniform scale), graph from the "
@@ -99,10 +108,11 @@ def config_data(name: str, nq_total: int):
     from beam_search_collab_b200 import datasets as ds
     cfg = CONFIGS[name]
     s = getattr(ds, cfg["gen"])(nq=nq_total)
-    graph = os.path.join(DATA_DIR, name, "graph.bin")
+    ddir = os.path.join(DATA_DIR, cfg.get("data_dir", name))
+    graph = os.path.join(ddir, "graph.bin")
     if not os.path.exists(graph):
         raise SystemExit(f"missing {graph}: build it with the reference build_graph over the {name} base")
-    cb = os.path.join(DATA_DIR, name, "codebook.bin") if cfg["codebook"] else None
+    cb = os.path.join(ddir, "codebook.bin") if cfg["codebook"] else None
     if cb and not os.path.exists(cb):
         # too large to ship (2.4 GB for C3): the reference build_rabitq makes it here
         sys.path.insert(0, os.path.join(ROOT, "oracle"))
@@ -346,11 +356,12 @@ def run_ours(args, rank, world, local_rank):
     if args.mode == "rabitq":
         # per expansion: adjacency row, the neighbours' 1-bit codes (pdim/8 B
         # each) and 3 f32 factors each, and the parent's exact row; then the
-        # exact rerank rows of the final beam
+        # exact rerank rows of the final beam.  The node blocks carry exactly
+        # these (padded to 16 B), one bulk copy per expansion.
         pdim = 1 << (dim - 1).bit_length()
-        per_expansion = (st.expansions * (4 * deg + deg * pdim // 8 + 12 * deg + st.row_bytes)
-                         + st.rerank * st.row_bytes)
-        useful = per_expansion
+        useful = (st.expansions * (4 * deg + deg * pdim // 8 + 12 * deg + st.row_bytes)
+                  + st.rerank * st.row_bytes)
+        per_expansion = (st.expansions * st.block_bytes + st.rerank * st.row_bytes) if st.block_bytes else useful
     elif st.block_bytes:
         per_expansion = st.expansions * st.block_bytes
         # the bytes the search needs in the stored row format: adjacency rows
@@ -469,7 +480,9 @@ def run_ours(args, rank, world, local_rank):
             "queries_per_gpu": nq,
             "distance_path": ("integer-exact" if st.integer_exact else "sequential per lane")
                              + f", stored row {st.row_bytes} B",
-            "layout": (f"neighbourhood blocks, {st.block_bytes} B bulk copy per expansion"
+            "layout": ((f"RaBitQ node blocks (adjacency, codes, factors, own row), {st.block_bytes} B bulk copy "
+                        "per expansion" if args.mode == "rabitq" else
+                        f"neighbourhood blocks, {st.block_bytes} B bulk copy per expansion")
                        if st.block_bytes else "gather"),
             "expansions_per_query": round(st.expansions / nq, 2),
             "distances_per_query": round(st.distances / nq, 2),
@@ -545,7 +558,7 @@ def _write_inputs(tmp, base, queries):
     bp, qp = os.path.join(tmp, "base.fvecs"), os.path.join(tmp, "query.fvecs")
     ds.write_fvecs(bp, base)
     ds.write_fvecs(qp, queries)
-    return os.path.join(DATA_DIR, CFG_NAME, "graph.bin"), bp, qp
+    return os.path.join(DATA_DIR, CONFIGS[CFG_NAME].get("data_dir", CFG_NAME), "graph.bin"), bp, qp
 
 
 def _ref_search(paths, topk, entry, nq, codebook=None, out=None):
@@ -638,7 +651,7 @@ def profile_run(args):
         # the builder's kernels: `warmup` builds and one more
         from beam_search_collab_b200 import datasets as ds
         s = getattr(ds, CONFIGS[CFG_NAME]["gen"])(nq=1)
-        ix = B.Index.from_arrays(s.base, ds.read_graph(os.path.join(DATA_DIR, CFG_NAME, "graph.bin")))
+        ix = B.Index.from_arrays(s.base, ds.read_graph(os.path.join(DATA_DIR, CONFIGS[CFG_NAME].get("data_dir", CFG_NAME), "graph.bin")))
         for _ in range(args.warmup + 1):
             ix.build_codebook(12345)
         torch.cuda.synchronize()
@@ -673,7 +686,7 @@ def measure_codebook(args):
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
     s = getattr(ds, CONFIGS[CFG_NAME]["gen"])(nq=1)
-    graph = os.path.join(DATA_DIR, CFG_NAME, "graph.bin")
+    graph = os.path.join(DATA_DIR, CONFIGS[CFG_NAME].get("data_dir", CFG_NAME), "graph.bin")
     ix = B.Index.from_arrays(s.base, ds.read_graph(graph))
     n, dim, deg = ix.info()
     for _ in range(args.warmup):

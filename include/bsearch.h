@@ -85,8 +85,9 @@ typedef struct bs_stats {
     uint32_t entry_point;     /* entry node the search used                   */
     uint32_t integer_exact;   /* 1: integer-exact distance path was used       */
     uint32_t row_bytes;       /* bytes per base row as stored on the device   */
-    uint32_t block_bytes;     /* bytes per neighbourhood block copied per
-                                 expansion (0: the gather layout was used)   */
+    uint32_t block_bytes;     /* bytes per node block copied per expansion
+                                 (neighbourhood block, or the RaBitQ node
+                                 block; 0: the gather layout was used)       */
     uint32_t reserved;
 } bs_stats;
 
