@@ -69,7 +69,7 @@ class Stats(ctypes.Structure):
 # Every symbol include/bsearch.h declares (checked by the CPU test suite).
 EXPORTS = ("bs_search_params_default", "bs_index_create", "bs_index_load", "bs_index_attach_rabitq",
            "bs_index_load_codebook", "bs_index_build_codebook", "bs_index_info", "bs_index_entry_point", "bs_index_rabitq_entry",
-           "bs_index_take_errors", "bs_index_destroy", "bs_search", "bs_search_no_alloc", "bs_merge_shards", "bs_device_alloc",
+           "bs_index_prepare", "bs_index_take_errors", "bs_index_destroy", "bs_search", "bs_search_no_alloc", "bs_merge_shards", "bs_device_alloc",
            "bs_device_free",
            "bs_copy_to_device",
            "bs_copy_to_host", "bs_device_fill", "bs_synchronize", "bs_last_error", "bs_version")
@@ -98,6 +98,7 @@ def lib() -> ctypes.CDLL:
     L.bs_index_entry_point.argtypes = [vp, _u32p]
     L.bs_index_rabitq_entry.argtypes = [vp, _u32p]
     L.bs_index_take_errors.argtypes = [vp, vp, _u32p]
+    L.bs_index_prepare.argtypes = [vp, ctypes.c_char_p]
     L.bs_index_destroy.argtypes = [vp]
     L.bs_index_destroy.restype = None
     L.bs_search.argtypes = [vp, ctypes.POINTER(_Params), vp, ctypes.c_uint32, vp, vp,
@@ -115,7 +116,7 @@ def lib() -> ctypes.CDLL:
     L.bs_synchronize.argtypes = [vp, vp]
     for f in ("bs_index_create", "bs_index_load", "bs_index_attach_rabitq", "bs_index_load_codebook",
               "bs_index_build_codebook",
-              "bs_index_info", "bs_index_entry_point", "bs_index_rabitq_entry", "bs_index_take_errors", "bs_search",
+              "bs_index_info", "bs_index_entry_point", "bs_index_rabitq_entry", "bs_index_take_errors", "bs_index_prepare", "bs_search",
               "bs_device_alloc", "bs_device_free", "bs_copy_to_device", "bs_copy_to_host",
               "bs_device_fill", "bs_synchronize"):
         getattr(L, f).restype = st
@@ -229,6 +230,10 @@ class Index:
         e = ctypes.c_uint32()
         _check(lib().bs_index_entry_point(self._h, ctypes.byref(e)))
         return e.value
+
+    def prepare(self, mode: str = "warp4") -> None:
+        """Builds the device layout `mode` searches on (bs_index_prepare)."""
+        _check(lib().bs_index_prepare(self._h, mode.encode()))
 
     def take_errors(self, stream: int = 0) -> int:
         """Kernel error bits reported by searches on this index since the last

@@ -49,6 +49,7 @@ struct bs_index {
     // when they fit comfortably in device memory
     unsigned char* d_nb = nullptr;
     uint32_t nb_stride = 0, nb_adj_bytes = 0, nb_pitch = 0;
+    bool nb_tried = false;       // the blocks are built on first need (or never)
     bool int_exact = false;      // every base value an integer
     std::vector<uint64_t> neg_zeros;  // byte rows: flat positions of -0.0 values (ascending)
     float min_val = 0.0f;        // range of the base values
@@ -267,6 +268,7 @@ void pack_u8_rows(const float* v, uint64_t n, int32_t dim, uint32_t row_bytes, u
 // units for f32 rows so that lanes reading one row each hit distinct banks
 // (u8 rows rotate their chunks instead).
 cudaError_t build_blocks(bs_index* ix) {
+    ix->nb_tried = true;
     const char* env = std::getenv("BSEARCH_LAYOUT");
     if (env && std::strcmp(env, "gather") == 0) return cudaSuccess;
     if (ix->degree > 64) return cudaSuccess;                    // the search supports degree <= 64
@@ -306,6 +308,15 @@ cudaError_t build_blocks(bs_index* ix) {
     cudaError_t e = bsb::build_neighbourhood_blocks(p, ix->d_nb, nullptr);
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     return e;
+}
+
+// The neighbourhood blocks of the exact and Bloom modes, built once, on the
+// first search that can use them (a RaBitQ-only index never pays their
+// memory).  Called with ix->mu held.
+bs_status ensure_blocks(bs_index* ix) {
+    if (ix->nb_tried) return BS_OK;
+    const cudaError_t e = build_blocks(ix);
+    return e == cudaSuccess ? BS_OK : cuda_fail(e, "neighbourhood blocks");
 }
 
 // RaBitQ node blocks [adjacency | codes | factors | own row] (16-byte aligned
@@ -612,7 +623,6 @@ BS_API bs_status bs_index_create(const bs_graph_desc* desc, int device, bs_index
     }
     if (e == cudaSuccess) e = cudaMemcpy(ix->d_adj, desc->edges, ebytes, cudaMemcpyHostToDevice);
     if (e != cudaSuccess) { free_index(ix); return cuda_fail(e, "index upload"); }
-    if ((e = build_blocks(ix)) != cudaSuccess) { free_index(ix); return cuda_fail(e, "neighbourhood blocks"); }
     // Per-call scratch comes from the device's stream-ordered pool: keep freed
     // blocks cached instead of returning them at every synchronisation.
     cudaMemPool_t pool;
@@ -832,6 +842,20 @@ BS_API bs_status bs_index_rabitq_entry(const bs_index* ix, uint32_t* entry) {
     return BS_OK;
 }
 
+BS_API bs_status bs_index_prepare(bs_index* ix, const char* mode) {
+    if (!ix) return fail(BS_ERR_INVALID_ARGUMENT, "index is NULL");
+    ModeInfo mi;
+    if (!parse_mode(mode, mi)) return fail(BS_ERR_INVALID_ARGUMENT, "Unknown mode: %s", mode ? mode : "(null)");
+    DeviceGuard g(ix->device);
+    if (!g.ok) return fail(BS_ERR_CUDA, "cannot select device %d", ix->device);
+    if (mi.rabitq) {
+        if (!ix->has_rabitq) return fail(BS_ERR_INVALID_ARGUMENT, "rabitq mode requires a codebook on the index");
+        return BS_OK;
+    }
+    std::lock_guard<std::mutex> lk(ix->mu);
+    return ensure_blocks(ix);
+}
+
 BS_API bs_status bs_index_take_errors(bs_index* ix, void* stream_, uint32_t* flags) {
     if (!ix || !flags) return fail(BS_ERR_INVALID_ARGUMENT, "index or flags is NULL");
     DeviceGuard g(ix->device);
@@ -874,6 +898,11 @@ BS_API bs_status bs_search(bs_index* ix, const bs_search_params* prm, const floa
         }
     }
     if (entry >= ix->n) return fail(BS_ERR_INVALID_ARGUMENT, "entry point %u out of range", entry);
+    if (!mi.rabitq) {
+        std::lock_guard<std::mutex> lk(ix->mu);
+        const bs_status bs = ensure_blocks(ix);
+        if (bs != BS_OK) return bs;
+    }
 
     SearchParams p;
     LaunchShape shape;
@@ -1049,7 +1078,8 @@ BS_API bs_status bs_search_no_alloc(bs_index* ix, const bs_search_params* prm, c
     if (!parse_mode(prm->mode, mi)) return fail(BS_ERR_INVALID_ARGUMENT, "Unknown mode: %s", prm->mode ? prm->mode : "(null)");
     if (mi.rabitq)
         return fail(BS_ERR_UNSUPPORTED,
-                    "rabitq needs per-warp visited-set spill tables larger than the %zu-byte fixed scratch; use bs_search",
+                    "rabitq needs visited bitmaps over all node ids per warp, far beyond the %zu-byte fixed scratch; "
+                    "use bs_search",
                     kFixedScratchBytes);
     if (prm->K <= 0) return fail(BS_ERR_INVALID_ARGUMENT, "K must be positive");
     if (prm->topk_size == 0) return fail(BS_ERR_INVALID_ARGUMENT, "topk_size must be positive");

@@ -93,6 +93,15 @@ CONFIGS = {
                           "RaBitQ codebook (build_rabitq seed 12345), K=10, exact rerank",
                  data="synthetic: seeded C2 mixture (1,024 Gaussians, ints 0..255), graph and codebook from the "
                       "reference build_graph / build_rabitq"),
+    # a 200,000-row slice of the C2 distribution with its own graph and
+    # codebook (reference tools): small enough for full ncu captures of the
+    # search kernels (a few hundred MB on the device), rows still beyond L2
+    "c2s": dict(gen="gen_c2", gen_kwargs={"n": 200_000}, nq=10_000, mode="rabitq", K=10,
+                sweep=(32, 48, 56, 64, 96, 128, 192, 256), codebook=True,
+                workload="C2 slice for profiling: 200k x 128 int-valued base, 10k queries, degree-32 Vamana, "
+                         "RaBitQ codebook (build_rabitq seed 12345), K=10",
+                data="synthetic: seeded C2 mixture (1,024 Gaussians, ints 0..255) at 200k rows, graph and "
+                     "codebook from the reference build_graph / build_rabitq"),
     "c4": dict(gen="gen_c4", nq=1_000, mode="base", K=100, sweep=(256,), codebook=False,
                workload="C4: 1M x 960 non-negative base, 1k queries per GPU, degree-32 Vamana, K=100, topk 256",
                data="synthetic: seeded C4 (|N(0,1)| * 0.1 * per-dimension log-uniform scale), graph from the "
@@ -107,7 +116,7 @@ def config_data(name: str, nq_total: int):
     bench_data/<config>/ (git-ignored, shipped to the GPU box)."""
     from beam_search_collab_b200 import datasets as ds
     cfg = CONFIGS[name]
-    s = getattr(ds, cfg["gen"])(nq=nq_total)
+    s = getattr(ds, cfg["gen"])(nq=nq_total, **cfg.get("gen_kwargs", {}))
     ddir = os.path.join(DATA_DIR, cfg.get("data_dir", name))
     graph = os.path.join(ddir, "graph.bin")
     if not os.path.exists(graph):
@@ -650,7 +659,7 @@ def profile_run(args):
     if args.measure == "codebook":
         # the builder's kernels: `warmup` builds and one more
         from beam_search_collab_b200 import datasets as ds
-        s = getattr(ds, CONFIGS[CFG_NAME]["gen"])(nq=1)
+        s = getattr(ds, CONFIGS[CFG_NAME]["gen"])(nq=1, **CONFIGS[CFG_NAME].get("gen_kwargs", {}))
         ix = B.Index.from_arrays(s.base, ds.read_graph(os.path.join(DATA_DIR, CONFIGS[CFG_NAME].get("data_dir", CFG_NAME), "graph.bin")))
         for _ in range(args.warmup + 1):
             ix.build_codebook(12345)
@@ -685,7 +694,7 @@ def measure_codebook(args):
     from beam_search_collab_b200 import datasets as ds
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
-    s = getattr(ds, CONFIGS[CFG_NAME]["gen"])(nq=1)
+    s = getattr(ds, CONFIGS[CFG_NAME]["gen"])(nq=1, **CONFIGS[CFG_NAME].get("gen_kwargs", {}))
     graph = os.path.join(DATA_DIR, CONFIGS[CFG_NAME].get("data_dir", CFG_NAME), "graph.bin")
     ix = B.Index.from_arrays(s.base, ds.read_graph(graph))
     n, dim, deg = ix.info()

@@ -133,6 +133,17 @@ BS_API bs_status bs_index_entry_point(bs_index* index, uint32_t* entry);
  * codebook is attached (reference src/gpu_cli.cu:436-437). */
 BS_API bs_status bs_index_rabitq_entry(const bs_index* index, uint32_t* entry);
 
+/* No counterpart in the reference.  Builds the device layout the exact and
+ * Bloom modes search fastest on (one contiguous neighbourhood block per node:
+ * its adjacency row and its neighbours' rows, one bulk copy per expansion;
+ * C2: 4.2 KB per node), when it fits in 40% of the free device memory.
+ * bs_search does this on its first exact or Bloom search; call it at set-up
+ * to take that cost out of the first search, or before bs_search_no_alloc,
+ * which never builds it (until then it searches the plain layout, with the
+ * same results).  A RaBitQ-only index never needs it.  "rabitq" checks that
+ * a codebook is attached (its node blocks are built when it is attached). */
+BS_API bs_status bs_index_prepare(bs_index* index, const char* mode);
+
 /* No counterpart in the reference, whose kernels have no error channel.
  * Every search kernel on this index also ORs its error bits (the ones
  * bs_search reports as BS_ERR_KERNEL) into a word held by the index, so that a
@@ -172,9 +183,13 @@ BS_API bs_status bs_search(bs_index* index, const bs_search_params* params, cons
  * first computed) lives in one 16 KiB file-scope device array that every GPU
  * loading the library holds until the process exits.
  *   - queries, ids and dists (NULL allowed) must be device pointers;
- *   - nq <= 2^31; "rabitq" is rejected (its visited-set spill tables need more
- *     than the fixed scratch), as is computing the entry point for
- *     dim > 4028 (pass entry_point or call bs_index_entry_point first);
+ *   - nq <= 2^31; "rabitq" is rejected (its never-forgetting visited sets
+ *     need a bitmap over all node ids per resident warp, far more than the
+ *     fixed scratch), as is computing the entry point for dim > 4028 (pass
+ *     entry_point or call bs_index_entry_point first);
+ *   - it searches the layout the index already has: the neighbourhood blocks
+ *     once bs_index_prepare (or an exact or Bloom bs_search) built them, else
+ *     the plain layout, with the same results;
  *   - the first call on a device looks up the array's device address, and if
  *     neither entry_point nor a cached entry is available it computes the
  *     entry point and synchronises `stream`; make that first call before any

@@ -72,6 +72,7 @@ def main():
     ap.add_argument("--modes", nargs="*", default=list(REF_MODES))
     ap.add_argument("--our-modes", nargs="*", default=list(OUR_MODES))
     ap.add_argument("--topks", nargs="*", type=int, default=list(TOPKS))
+    ap.add_argument("--codebook", default=None, help="codebook.bin of the C2 graph (rabitq runs)")
     a = ap.parse_args()
     if not os.access(REF_CLI, os.X_OK):
         raise SystemExit("oracle/_ref/gpu_cli is not built (make -C oracle gpu REF=<reference tree>)")
@@ -89,6 +90,12 @@ def main():
         ds.write_fvecs(data["base"], s.base)
         ds.write_fvecs(data["query"], s.queries)
         ds.write_ivecs(data["gt"], gt)
+        if a.codebook:
+            if not os.path.exists(a.codebook):
+                # the reference builder, seed 12345 (as the benchmark's C2+RaBitQ workload)
+                subprocess.run([os.path.join(HERE, "_ref", "build_rabitq"), "-base", data["base"], "-graph", graph,
+                                "-out", a.codebook, "-seed", "12345"], check=True, stdout=subprocess.DEVNULL)
+            data["codebook"] = a.codebook
         plan = [("reference", REF_CLI, m) for m in a.modes] + [("ours", OUR_CLI, m) for m in a.our_modes]
         for impl, cli, mode in plan:
             for t in a.topks:
