@@ -50,6 +50,7 @@ struct bs_index {
     unsigned char* d_nb = nullptr;
     uint32_t nb_stride = 0, nb_adj_bytes = 0, nb_pitch = 0;
     bool nb_tried = false;       // the blocks are built on first need (or never)
+    bool gather_only = false;    // BSEARCH_LAYOUT=gather at creation: no blocks of any kind
     bool int_exact = false;      // every base value an integer
     std::vector<uint64_t> neg_zeros;  // byte rows: flat positions of -0.0 values (ascending)
     float min_val = 0.0f;        // range of the base values
@@ -269,8 +270,7 @@ void pack_u8_rows(const float* v, uint64_t n, int32_t dim, uint32_t row_bytes, u
 // (u8 rows rotate their chunks instead).
 cudaError_t build_blocks(bs_index* ix) {
     ix->nb_tried = true;
-    const char* env = std::getenv("BSEARCH_LAYOUT");
-    if (env && std::strcmp(env, "gather") == 0) return cudaSuccess;
+    if (ix->gather_only) return cudaSuccess;
     if (ix->degree > 64) return cudaSuccess;                    // the search supports degree <= 64
     uint32_t pitch;
     if (ix->u8) {
@@ -325,8 +325,7 @@ bs_status ensure_blocks(bs_index* ix) {
 cudaError_t build_rq_blocks(bs_index* ix) {
     cudaFree(ix->d_rqb);
     ix->d_rqb = nullptr;
-    const char* env = std::getenv("BSEARCH_LAYOUT");
-    if (env && std::strcmp(env, "gather") == 0) return cudaSuccess;
+    if (ix->gather_only) return cudaSuccess;
     if (ix->degree > 64) return cudaSuccess;
     auto a16 = [](uint64_t x) { return (x + 15u) & ~static_cast<uint64_t>(15u); };
     const uint64_t deg = static_cast<uint64_t>(ix->degree), wpp = static_cast<uint64_t>(ix->pdim) / 32u;
@@ -567,6 +566,10 @@ BS_API bs_status bs_index_create(const bs_graph_desc* desc, int device, bs_index
     auto* ix = new (std::nothrow) bs_index();
     if (!ix) return fail(BS_ERR_OUT_OF_MEMORY, "host allocation failed");
     ix->device = device;
+    {
+        const char* env = std::getenv("BSEARCH_LAYOUT");
+        ix->gather_only = env && std::strcmp(env, "gather") == 0;
+    }
     ix->n = desc->num_nodes;
     ix->dim = desc->dim;
     ix->degree = desc->degree;

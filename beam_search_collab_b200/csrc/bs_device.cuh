@@ -186,6 +186,123 @@ __device__ __forceinline__ void beam_merge_compact(uint64_t (&beam)[RX], const u
         if (static_cast<unsigned>(r) * 32u + lane >= topk) beam[r] = kEmptyKey;
 }
 
+// ---- the same networks with the lane-level stages (partner distance < 32)
+// as runtime loops: one copy of a stage's code instead of one per stage, for
+// kernels whose unrolled networks would not fit the instruction cache (wide
+// beams); the register-level stages stay unrolled (their register indices
+// must be constants).
+
+template <int N>
+__device__ __forceinline__ void cmpx_shfl(uint64_t (&k)[N], unsigned lane, unsigned size, unsigned stride) {
+    const bool lower = (lane & stride) == 0;
+#pragma unroll
+    for (int r = 0; r < N; ++r) {
+        const uint64_t o = __shfl_xor_sync(kFull, k[r], stride);
+        const unsigned p = static_cast<unsigned>(r) * 32u + lane;
+        const bool asc = (p & size) == 0;
+        k[r] = (asc == lower) ? kmin(k[r], o) : kmax(k[r], o);
+    }
+}
+
+template <int N, unsigned SIZE, unsigned STRIDE>
+__device__ __forceinline__ void merge_reg_stages(uint64_t (&k)[N], unsigned lane) {
+    if constexpr (STRIDE >= 32) {
+        cmpx_stage<N, SIZE, STRIDE>(k, lane);
+        merge_reg_stages<N, SIZE, STRIDE / 2>(k, lane);
+    }
+}
+
+// bitonic merge of blocks of SIZE keys (SIZE a power of two, <= 32*N)
+template <int N, unsigned SIZE>
+__device__ __forceinline__ void merge_rt(uint64_t (&k)[N], unsigned lane) {
+    merge_reg_stages<N, SIZE, SIZE / 2>(k, lane);
+#pragma unroll 1
+    for (unsigned stride = (SIZE / 2 < 16u ? SIZE / 2 : 16u); stride > 0; stride >>= 1)
+        cmpx_shfl<N>(k, lane, SIZE, stride);
+}
+
+template <int N, unsigned SIZE>
+__device__ __forceinline__ void sort_big_rt(uint64_t (&k)[N], unsigned lane) {
+    if constexpr (SIZE >= 64) {
+        sort_big_rt<N, SIZE / 2>(k, lane);
+        merge_rt<N, SIZE>(k, lane);
+    }
+}
+
+// ascending sort of blocks of SIZE keys (the whole array for SIZE = 32*N)
+template <int N, unsigned SIZE>
+__device__ __forceinline__ void sort_rt(uint64_t (&k)[N], unsigned lane) {
+    constexpr unsigned kLane = SIZE < 32u ? SIZE : 32u;
+#pragma unroll 1
+    for (unsigned size = 2; size <= kLane; size <<= 1)
+#pragma unroll 1
+        for (unsigned stride = size >> 1; stride > 0; stride >>= 1) cmpx_shfl<N>(k, lane, size, stride);
+    sort_big_rt<N, SIZE>(k, lane);
+}
+
+// beam_merge_compact for wide beams (RaBitQ: topk up to 512).  Up to kIns
+// keys are shifted in one at a time.  Otherwise the keys are sorted and paired
+// with the beam's last rows as in beam_merge_compact; every beam row whose
+// largest key is at or below the smallest candidate is left alone (all its
+// keys precede every candidate), and the bitonic merge runs only over the
+// smallest power-of-two suffix of rows that holds the others.  That suffix,
+// an ascending run whose tail was min-paired with the reversed candidates, is
+// bitonic, so merging it alone sorts the whole beam.
+template <int RX, int S>
+__device__ __forceinline__ void merge_suffix(uint64_t (&beam)[RX], unsigned lane) {
+    uint64_t sub[S];
+#pragma unroll
+    for (int i = 0; i < S; ++i) sub[i] = beam[RX - S + i];
+    merge_rt<S, 32u * S>(sub, lane);
+#pragma unroll
+    for (int i = 0; i < S; ++i) beam[RX - S + i] = sub[i];
+}
+
+template <int RX, int RY>
+__device__ __forceinline__ void beam_merge_compact_wide(uint64_t (&beam)[RX], const uint64_t* ckeys,
+                                                        unsigned count, unsigned lane, unsigned topk) {
+    constexpr unsigned kIns = RX >= 4 ? 3u : 2u;
+    if (count <= kIns) {
+        for (unsigned j = 0; j < count; ++j) beam_insert1<RX>(beam, lane, ckeys[j], topk);
+        return;
+    }
+    uint64_t cand[RY];
+#pragma unroll
+    for (int r = 0; r < RY; ++r) {
+        const unsigned s = static_cast<unsigned>(r) * 32u + lane;
+        cand[r] = s < count ? ckeys[s] : kEmptyKey;
+    }
+    if (count <= 32) {
+        // sort the first register row in blocks of the smallest power of two
+        // that holds the keys (empty slots hold kEmptyKey, the largest key)
+        unsigned size = 8;
+        while (size < count) size <<= 1;
+#pragma unroll 1
+        for (unsigned sz = 2; sz <= size; sz <<= 1)
+#pragma unroll 1
+            for (unsigned stride = sz >> 1; stride > 0; stride >>= 1) cmpx_shfl<RY>(cand, lane, sz, stride);
+    } else {
+        sort_rt<RY, 32u * RY>(cand, lane);
+    }
+    const uint64_t cmin = __shfl_sync(kFull, cand[0], 0);
+    int r0 = RX;
+#pragma unroll
+    for (int r = RX - 1; r >= 0; --r)
+        if (__shfl_sync(kFull, beam[r], 31) > cmin) r0 = r;
+#pragma unroll
+    for (int r = RX - RY; r < RX; ++r) {
+        const uint64_t c = __shfl_xor_sync(kFull, cand[RX - 1 - r], 31);
+        beam[r] = kmin(beam[r], c);
+    }
+    if (RX >= 2 && RY <= 1 && r0 >= RX - 1) merge_suffix<RX, 1>(beam, lane);
+    else if (RX >= 4 && RY <= 2 && r0 >= RX - 2) merge_suffix<RX, (RX >= 4 ? 2 : 1)>(beam, lane);
+    else if (RX >= 8 && r0 >= RX - 4) merge_suffix<RX, (RX >= 8 ? 4 : 1)>(beam, lane);
+    else merge_rt<RX, 32u * RX>(beam, lane);
+#pragma unroll
+    for (int r = 0; r < RX; ++r)
+        if (static_cast<unsigned>(r) * 32u + lane >= topk) beam[r] = kEmptyKey;
+}
+
 // Smallest unexpanded entry: mark it and return its node id.  Branch-free
 // over the registers so the beam stays in registers.
 template <int RX>

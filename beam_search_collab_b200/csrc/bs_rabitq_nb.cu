@@ -157,8 +157,14 @@ __device__ __forceinline__ uint32_t raw_sum(const uint32_t* code, uint32_t wpp, 
     return raw;
 }
 
+// Resident blocks of 4 warps per SM the register budget is fitted to (6:
+// 85 registers a thread) for beams up to 256 entries.
+#ifndef BS_RQ_MIN_BLOCKS
+#define BS_RQ_MIN_BLOCKS 6
+#endif
+
 template <int RX, int RY, int DM, int EM>
-__global__ void __launch_bounds__(128, (RX <= 8 ? 6 : 4)) k_search_rq_nb(const SearchParams p) {
+__global__ void __launch_bounds__(128, (RX <= 8 ? BS_RQ_MIN_BLOCKS : 4)) k_search_rq_nb(const SearchParams p) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const unsigned lane = threadIdx.x & 31u;
     unsigned char* ws = smem_raw + static_cast<size_t>(threadIdx.x >> 5) * p.smem_per_warp;
@@ -257,17 +263,25 @@ __global__ void __launch_bounds__(128, (RX <= 8 ? 6 : 4)) k_search_rq_nb(const S
                 lut[e] = static_cast<uint16_t>(s);
             }
         }
-        if (lane == 0) cids[0] = p.entry;
         __syncwarp();
 
-        // ---- seed (the block buffer stages the entry's row)
-        score_rows<DM>(p, 1, cids, cdist, qsm, q8, reinterpret_cast<float*>(blk), lane, team_ok);
+        // ---- seed: the entry's row into the block buffer's row slot, then
+        // the same fold as for an expanded node
+        {
+            const uint32_t words = (DM == kU8 ? p.row_bytes : p.row_stride * 4u) / 4u;
+            const uint32_t* src = DM == kU8 ? reinterpret_cast<const uint32_t*>(p.vecs8 + static_cast<size_t>(p.entry) * p.row_bytes)
+                                            : reinterpret_cast<const uint32_t*>(p.vecs + static_cast<size_t>(p.entry) * p.row_stride);
+            uint32_t* dst = reinterpret_cast<uint32_t*>(blk_row);
+            for (uint32_t i = lane; i < words; i += 32) dst[i] = src[i];
+            __syncwarp();
+        }
+        const float entry_d = block_exact<DM>(p, blk_row, qsm, q8, team_ok, lane);
         uint64_t beam[RX];
 #pragma unroll
         for (int r = 0; r < RX; ++r) beam[r] = kEmptyKey;
         uint32_t logged = 1;
         if (lane == 0) {
-            beam[0] = make_key(cdist[0], p.entry);
+            beam[0] = make_key(entry_d, p.entry);
             visit(vbits, p.entry);
             vlog[0] = p.entry;
         }
@@ -296,49 +310,53 @@ __global__ void __launch_bounds__(128, (RX <= 8 ? 6 : 4)) k_search_rq_nb(const S
             }
             phase ^= 1u;
 
-            // test-and-set every neighbour's bit (the atomics are in flight
-            // while the expanded node's own distance is folded)
-            uint32_t c[RY];
-            bool fresh[RY];
+            // test-and-set every neighbour's bit; the returned words are
+            // first needed after the own-row fold and the estimates, which
+            // are computed for every neighbour meanwhile
+            uint32_t c[RY], old[RY];
 #pragma unroll
             for (int r = 0; r < RY; ++r) {
                 const uint32_t pos = static_cast<uint32_t>(r) * 32u + lane;
                 c[r] = pos < deg ? blk_adj[pos] : kNoNode;
-                fresh[r] = c[r] < p.n && visit(vbits, c[r]);
+                old[r] = c[r] < p.n ? atomicOr(vbits + (c[r] >> 5), 1u << (c[r] & 31u)) : ~0u;
             }
             // exact distance of the expanded node (include/cpu_search_rabitq.hpp:130)
             const float exact = block_exact<DM>(p, blk_row, qsm, q8, team_ok, lane);
             ++D;
 
-            // log the ids set here; estimate them
+            float est[RY];
+#pragma unroll
+            for (int r = 0; r < RY; ++r) {
+                // include/cpu_search_rabitq.hpp:72-97
+                const uint32_t pos = static_cast<uint32_t>(r) * 32u + lane;
+                est[r] = FLT_MAX;
+                const float tx = pos < deg ? blk_fac[pos] : FLT_MAX;
+                if (tx != FLT_MAX) {
+                    const float fdq = blk_fac[deg + pos];
+                    const float fvq = blk_fac[2u * deg + pos];
+                    const uint32_t raw = raw_sum<EM>(blk_codes + pos * wpp, wpp, est_tab);
+                    const float ip = static_cast<float>((static_cast<int32_t>(raw) << 1) - sum_q);
+                    const float e = __fadd_rn(__fadd_rn(__fadd_rn(tx, exact), __fmul_rn(__fmul_rn(fdq, w), ip)),
+                                              __fmul_rn(fvq, lo));
+                    est[r] = isfinite(e) ? e : FLT_MAX;
+                }
+            }
+
+            // the neighbours whose bit was new: log them, keep their estimates
             uint64_t k[RY];
             bool keep[RY];
             const uint64_t bound = beam_bound<RX>(beam, p.topk);
 #pragma unroll
             for (int r = 0; r < RY; ++r) {
-                const unsigned b = __ballot_sync(kFull, fresh[r]);
-                if (fresh[r]) {
+                const bool fresh = (old[r] & (1u << (c[r] & 31u))) == 0u;
+                const unsigned b = __ballot_sync(kFull, fresh);
+                if (fresh) {
                     const uint32_t at = logged + __popc(b & lt_mask);
                     if (at < p.vis_log_cap) vlog[at] = c[r];
                 }
                 logged += __popc(b);
                 EST += __popc(b);
-                float est = FLT_MAX;
-                if (fresh[r]) {
-                    // include/cpu_search_rabitq.hpp:72-97
-                    const uint32_t pos = static_cast<uint32_t>(r) * 32u + lane;
-                    const float tx = blk_fac[pos];
-                    if (tx != FLT_MAX) {
-                        const float fdq = blk_fac[deg + pos];
-                        const float fvq = blk_fac[2u * deg + pos];
-                        const uint32_t raw = raw_sum<EM>(blk_codes + pos * wpp, wpp, est_tab);
-                        const float ip = static_cast<float>((static_cast<int32_t>(raw) << 1) - sum_q);
-                        const float e = __fadd_rn(__fadd_rn(__fadd_rn(tx, exact), __fmul_rn(__fmul_rn(fdq, w), ip)),
-                                                  __fmul_rn(fvq, lo));
-                        est = isfinite(e) ? e : FLT_MAX;
-                    }
-                }
-                k[r] = fresh[r] ? make_key(est, c[r]) : kEmptyKey;
+                k[r] = fresh ? make_key(est[r], c[r]) : kEmptyKey;
                 keep[r] = k[r] < bound;
             }
 
@@ -351,7 +369,7 @@ __global__ void __launch_bounds__(128, (RX <= 8 ? 6 : 4)) k_search_rq_nb(const S
             }
             if (cnt) {
                 __syncwarp();
-                beam_merge_compact<RX, RY>(beam, ckeys, cnt, lane, p.topk);
+                beam_merge_compact_wide<RX, RY>(beam, ckeys, cnt, lane, p.topk);
             }
         }
 
@@ -362,17 +380,15 @@ __global__ void __launch_bounds__(128, (RX <= 8 ? 6 : 4)) k_search_rq_nb(const S
 #pragma unroll
         for (int r = 0; r < RX; ++r) {
             const bool v = beam[r] != kEmptyKey;
-            const uint32_t cnt = __popc(__ballot_sync(kFull, v));   // valid entries form a prefix
-            if (cnt) {
-                __syncwarp();
-                if (v) cids[lane] = key_id(beam[r]);
-                __syncwarp();
-                score_rows<DM>(p, cnt, cids, cdist, qsm, q8, reinterpret_cast<float*>(blk), lane, team_ok);
-                if (v) beam[r] = make_key(cdist[lane], key_id(beam[r]));
-                rr += cnt;
-            }
+            if (v) cids[r * 32 + lane] = key_id(beam[r]);
+            rr += __popc(__ballot_sync(kFull, v));                 // valid entries form a prefix
         }
-        sort_asc<RX>(beam, lane);
+        __syncwarp();
+        if (rr) score_rows<DM>(p, rr, cids, cdist, qsm, q8, reinterpret_cast<float*>(blk), lane, team_ok);
+#pragma unroll
+        for (int r = 0; r < RX; ++r)
+            if (beam[r] != kEmptyKey) beam[r] = make_key(cdist[r * 32 + lane], key_id(beam[r]));
+        sort_rt<RX, 32u * RX>(beam, lane);
 
         uint32_t* oid = p.out_ids + static_cast<size_t>(qi) * p.K;
         float* odist = p.out_dists ? p.out_dists + static_cast<size_t>(qi) * p.K : nullptr;
@@ -533,10 +549,10 @@ cudaError_t plan_search_rq_nb(SearchParams& p, LaunchShape& shape, size_t max_sm
     if (shape.dmode == kU8) off = a16(off + p.row_bytes + 4u);
     p.off_est = off;
     off = a16(off + (p.rq_lut ? p.pdim * 8u : p.wpp * 32u));       // nibble table or bit-planes
-    p.off_cids = off;
-    off = a16(off + 32u * 4u);
+    p.off_cids = off;                                               // the final beam's ids
+    off = a16(off + 32u * static_cast<uint32_t>(shape.regx) * 4u);
     p.off_cdist = off;
-    off = a16(off + 32u * 4u);
+    off = a16(off + 32u * static_cast<uint32_t>(shape.regx) * 4u);
     p.off_keys = off;
     off = a16(off + 32u * static_cast<uint32_t>(shape.regy) * 8u);
     p.off_mbar = off;
