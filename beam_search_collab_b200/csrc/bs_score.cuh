@@ -62,7 +62,10 @@ __device__ __forceinline__ void score_rows_seq(const SearchParams& p, uint32_t m
 // in order with separately rounded operations: the reference's bits (the zero
 // pad of the stored rows and of the query adds +0).
 constexpr uint32_t kRingCh = 32;       // dimensions per chunk
-constexpr uint32_t kRingStages = 4;    // chunks in the ring (3 in flight while one is folded)
+#ifndef BS_RING_STAGES
+#define BS_RING_STAGES 4
+#endif
+constexpr uint32_t kRingStages = BS_RING_STAGES;  // chunks in the ring (all but one in flight while one is folded)
 constexpr uint32_t kRingPitch = 36;    // floats per staged row chunk: 9 16-byte units, odd
 constexpr uint32_t kRingFloats = kRingStages * 32u * kRingPitch;
 

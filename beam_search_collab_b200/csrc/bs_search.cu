@@ -360,6 +360,9 @@ cudaError_t plan_search(SearchParams& p, LaunchShape& shape, size_t max_smem_opt
             p.stage_ring = 1;
             p.stage_rows = 0;
             off = align16(off + dev::kRingFloats * 4u);
+            // tens of KB per warp: one warp per block, so that the SM's shared
+            // memory holds as many warps (queries) as fit, not whole blocks
+            shape.warps_per_block = 1;
         } else {
             off = align16(off + rows * row_bytes);
         }
