@@ -49,6 +49,10 @@ class _RabitqDesc(ctypes.Structure):
                 ("codes", ctypes.c_void_p), ("factors", ctypes.c_void_p), ("signs", ctypes.c_void_p)]
 
 
+class _BuildParams(ctypes.Structure):
+    _fields_ = [("beam_width", ctypes.c_int32), ("alpha", ctypes.c_float), ("seed", ctypes.c_uint32)]
+
+
 class _Params(ctypes.Structure):
     _fields_ = [("mode", ctypes.c_char_p), ("K", ctypes.c_int32), ("topk_size", ctypes.c_uint32),
                 ("filter_capacity", ctypes.c_uint32), ("max_iterations", ctypes.c_int32),
@@ -69,7 +73,7 @@ class Stats(ctypes.Structure):
 # Every symbol include/bsearch.h declares (checked by the CPU test suite).
 EXPORTS = ("bs_search_params_default", "bs_index_create", "bs_index_load", "bs_index_attach_rabitq",
            "bs_index_load_codebook", "bs_index_build_codebook", "bs_index_info", "bs_index_entry_point", "bs_index_rabitq_entry",
-           "bs_index_prepare", "bs_index_take_errors", "bs_index_destroy", "bs_search", "bs_search_no_alloc", "bs_merge_shards", "bs_device_alloc",
+           "bs_index_build_graph", "bs_index_prepare", "bs_index_take_errors", "bs_index_destroy", "bs_search", "bs_search_no_alloc", "bs_merge_shards", "bs_device_alloc",
            "bs_device_free",
            "bs_copy_to_device",
            "bs_copy_to_host", "bs_device_fill", "bs_synchronize", "bs_last_error", "bs_version")
@@ -99,6 +103,7 @@ def lib() -> ctypes.CDLL:
     L.bs_index_rabitq_entry.argtypes = [vp, _u32p]
     L.bs_index_take_errors.argtypes = [vp, vp, _u32p]
     L.bs_index_prepare.argtypes = [vp, ctypes.c_char_p]
+    L.bs_index_build_graph.argtypes = [vp, ctypes.POINTER(_BuildParams), _u32p]
     L.bs_index_destroy.argtypes = [vp]
     L.bs_index_destroy.restype = None
     L.bs_search.argtypes = [vp, ctypes.POINTER(_Params), vp, ctypes.c_uint32, vp, vp,
@@ -116,7 +121,7 @@ def lib() -> ctypes.CDLL:
     L.bs_synchronize.argtypes = [vp, vp]
     for f in ("bs_index_create", "bs_index_load", "bs_index_attach_rabitq", "bs_index_load_codebook",
               "bs_index_build_codebook",
-              "bs_index_info", "bs_index_entry_point", "bs_index_rabitq_entry", "bs_index_take_errors", "bs_index_prepare", "bs_search",
+              "bs_index_info", "bs_index_entry_point", "bs_index_rabitq_entry", "bs_index_take_errors", "bs_index_prepare", "bs_index_build_graph", "bs_search",
               "bs_device_alloc", "bs_device_free", "bs_copy_to_device", "bs_copy_to_host",
               "bs_device_fill", "bs_synchronize"):
         getattr(L, f).restype = st
@@ -182,6 +187,24 @@ class Index:
         h = ctypes.c_void_p()
         _check(lib().bs_index_create(ctypes.byref(d), device, ctypes.byref(h)))
         return cls(h.value)
+
+    @classmethod
+    def from_vectors(cls, vectors: np.ndarray, degree: int, device: int = 0) -> "Index":
+        """An index over `vectors` with no graph yet (for build_graph)."""
+        vectors = np.ascontiguousarray(vectors, dtype=np.float32)
+        d = _GraphDesc(vectors.shape[0], vectors.shape[1], degree, _ptr(vectors), None)
+        h = ctypes.c_void_p()
+        _check(lib().bs_index_create(ctypes.byref(d), device, ctypes.byref(h)))
+        return cls(h.value)
+
+    def build_graph(self, beam_width: int = 128, alpha: float = 2.0, seed: int = 1234) -> np.ndarray:
+        """Builds this index's graph on the GPU with the reference build_graph's
+        algorithm (src/build_graph.cpp:255-397); returns the edges [n, degree]."""
+        n, _, deg = self.info()
+        out = np.empty((n, deg), dtype=np.uint32)
+        p = _BuildParams(beam_width, alpha, seed)
+        _check(lib().bs_index_build_graph(self._h, ctypes.byref(p), out.ctypes.data_as(_u32p)))
+        return out
 
     @classmethod
     def load(cls, graph_bin: str, base_fvecs: str, device: int = 0) -> "Index":

@@ -1,6 +1,6 @@
 """Builds the native parts in-tree (no JIT cache): the sm_100a shared library
 ``lib/libbsearch_b200.so`` (C ABI of include/bsearch.h) and the drop-in CLIs
-``bin/gpu_cli`` and ``bin/build_rabitq``.
+``bin/gpu_cli``, ``bin/build_rabitq`` and ``bin/build_graph``.
 
     python -m beam_search_collab_b200.build [--force]
 
@@ -27,8 +27,9 @@ BIN_DIR = os.path.join(PKG, "bin")
 LIB = os.path.join(LIB_DIR, "libbsearch_b200.so")
 CLI = os.path.join(BIN_DIR, "gpu_cli")
 RQ_CLI = os.path.join(BIN_DIR, "build_rabitq")
+BG_CLI = os.path.join(BIN_DIR, "build_graph")
 
-CU_SOURCES = ["bs_search.cu", "bs_search_nb.cu", "bs_rabitq.cu", "bs_rabitq_nb.cu", "bs_entry.cu", "bs_merge.cu", "bs_codebook.cu",
+CU_SOURCES = ["bs_search.cu", "bs_search_nb.cu", "bs_rabitq.cu", "bs_rabitq_nb.cu", "bs_graph_build.cu", "bs_entry.cu", "bs_merge.cu", "bs_codebook.cu",
               "bs_capi.cu"]
 NVCC_FLAGS = ["-std=c++17", "-O3", "-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo",
               "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
@@ -97,6 +98,10 @@ def build(force: bool = False, verbose: bool = False) -> str:
     cli_src = os.path.join(CSRC, "gpu_cli.cpp")
     if force or _stale(CLI, [cli_src, LIB] + headers):
         _run([_cxx(), "-std=c++20", "-O2", "-Wall", "-I", INCLUDE, cli_src, "-o", CLI,
+              "-L", LIB_DIR, "-lbsearch_b200", "-Wl,-rpath,$ORIGIN/../lib"])
+    bg_src = os.path.join(CSRC, "build_graph_cli.cpp")
+    if force or _stale(BG_CLI, [bg_src, LIB] + headers):
+        _run([_cxx(), "-std=c++20", "-O2", "-Wall", "-I", INCLUDE, bg_src, "-o", BG_CLI,
               "-L", LIB_DIR, "-lbsearch_b200", "-Wl,-rpath,$ORIGIN/../lib"])
     rq_src = os.path.join(CSRC, "build_rabitq_cli.cpp")
     if force or _stale(RQ_CLI, [rq_src, LIB, os.path.join(INCLUDE, "bsearch.h")]):

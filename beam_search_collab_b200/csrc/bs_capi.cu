@@ -549,7 +549,7 @@ BS_API const char* bs_version(void) { return "beam_search_collab_b200 0.1 (sm_10
 BS_API bs_status bs_index_create(const bs_graph_desc* desc, int device, bs_index** out) {
     if (!out) return fail(BS_ERR_INVALID_ARGUMENT, "out is NULL");
     *out = nullptr;
-    if (!desc || !desc->vectors || !desc->edges) return fail(BS_ERR_INVALID_ARGUMENT, "graph descriptor or its arrays are NULL");
+    if (!desc || !desc->vectors) return fail(BS_ERR_INVALID_ARGUMENT, "graph descriptor or its vectors are NULL");
     if (desc->num_nodes == 0 || desc->dim <= 0 || desc->degree <= 0)
         return fail(BS_ERR_INVALID_ARGUMENT, "num_nodes, dim and degree must be positive");
     if (desc->num_nodes >= (1ull << 31))
@@ -624,7 +624,10 @@ BS_API bs_status bs_index_create(const bs_graph_desc* desc, int device, bs_index
                                  cudaMemcpyHostToDevice);
         }
     }
-    if (e == cudaSuccess) e = cudaMemcpy(ix->d_adj, desc->edges, ebytes, cudaMemcpyHostToDevice);
+    // no edges: an empty graph (node 0 in every slot, as build_graph pads)
+    // for bs_index_build_graph to fill
+    if (e == cudaSuccess)
+        e = desc->edges ? cudaMemcpy(ix->d_adj, desc->edges, ebytes, cudaMemcpyHostToDevice) : cudaMemset(ix->d_adj, 0, ebytes);
     if (e != cudaSuccess) { free_index(ix); return cuda_fail(e, "index upload"); }
     // Per-call scratch comes from the device's stream-ordered pool: keep freed
     // blocks cached instead of returning them at every synchronisation.
@@ -842,6 +845,134 @@ BS_API bs_status bs_index_entry_point(bs_index* ix, uint32_t* entry) {
 BS_API bs_status bs_index_rabitq_entry(const bs_index* ix, uint32_t* entry) {
     if (!ix || !entry) return fail(BS_ERR_INVALID_ARGUMENT, "index or entry is NULL");
     *entry = ix->has_rabitq ? ix->rq_entry : BS_NO_NODE;
+    return BS_OK;
+}
+
+BS_API bs_status bs_index_build_graph(bs_index* ix, const bs_graph_build_params* prm, uint32_t* edges_out) {
+    if (!ix || !prm) return fail(BS_ERR_INVALID_ARGUMENT, "index or params is NULL");
+    if (ix->degree > 64) return fail(BS_ERR_UNSUPPORTED, "the graph builder supports degree <= 64");
+    if (prm->beam_width <= 0 || prm->beam_width > 512)
+        return fail(BS_ERR_UNSUPPORTED, "beam_width must be in 1..512");
+    if (!(prm->alpha >= 1.0f)) return fail(BS_ERR_INVALID_ARGUMENT, "--alpha must be at least 1.0");
+    DeviceGuard g(ix->device);
+    if (!g.ok) return fail(BS_ERR_CUDA, "cannot select device %d", ix->device);
+    const uint64_t n = ix->n;
+    const uint32_t deg = static_cast<uint32_t>(ix->degree);
+    // insertion order: the reference's generator and shuffle
+    // (src/build_graph.cpp:298-301), from the same standard library
+    std::vector<uint32_t> order(n);
+    for (uint64_t i = 0; i < n; ++i) order[i] = static_cast<uint32_t>(i);
+    {
+        std::mt19937 gen(prm->seed);
+        std::shuffle(order.begin(), order.end(), gen);
+    }
+    bsb::GraphBuildArgs a{};
+    {
+        ModeInfo mi{false, bsb::kHash, 4};
+        bs_search_params sp0;
+        bs_search_params_default(&sp0);
+        LaunchShape shape;
+        fill_params(ix, mi, &sp0, 0, a.sp, shape);
+        a.sp.nb = nullptr;
+    }
+    a.degree = deg;
+    a.L = static_cast<uint32_t>(prm->beam_width);
+    a.alpha = prm->alpha;
+    if (bsb::plan_graph_build(a, ix->smem_optin) != cudaSuccess)
+        return fail(BS_ERR_UNSUPPORTED, "rows of %d dimensions do not fit the graph builder's shared memory", ix->dim);
+    const uint64_t bound = std::max<uint64_t>(1, static_cast<uint64_t>(0.02 * static_cast<double>(n)));
+    const uint64_t batch_max = std::max<uint64_t>(1, std::min<uint64_t>(bound, n > 1 ? n - 1 : 1));
+    constexpr uint32_t kPoolCap = 2048, kLogCap = 8192;
+    uint32_t cap_warps = bsb::graph_build_search_warps(a, ix->num_sms, ix->smem_optin);
+    if (cap_warps == 0) return fail(BS_ERR_UNSUPPORTED, "graph builder launch shape");
+    const uint32_t words = static_cast<uint32_t>(((n + 31u) / 32u + 3u) & ~3ull);
+    const uint64_t per_warp = (static_cast<uint64_t>(words) + kLogCap) * 4u;
+    size_t free_b = 0, total_b = 0;
+    cudaError_t e = cudaMemGetInfo(&free_b, &total_b);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemGetInfo");
+    uint64_t vis_warps = std::min<uint64_t>({cap_warps, (batch_max + 3) / 4 * 4, (free_b / 4u) / per_warp});
+    vis_warps -= vis_warps % 4;
+    if (vis_warps < 4) return fail(BS_ERR_OUT_OF_MEMORY, "graph builder visited sets do not fit");
+    const uint64_t items = batch_max * deg;
+    const size_t sort_bytes = bsb::graph_build_sort_bytes(items);
+    void* d_order = nullptr; void* d_dist = nullptr; void* d_cnt = nullptr; void* d_pool = nullptr;
+    void* d_pcnt = nullptr; void* d_vis = nullptr; void* d_rev = nullptr; void* d_sort = nullptr;
+    void* d_misc = nullptr;
+    auto cleanup = [&]() {
+        for (void* q : {d_order, d_dist, d_cnt, d_pool, d_pcnt, d_vis, d_rev, d_sort, d_misc}) cudaFree(q);
+    };
+    if ((e = cudaMalloc(&d_order, n * 4)) != cudaSuccess || (e = cudaMalloc(&d_dist, n * deg * 4)) != cudaSuccess ||
+        (e = cudaMalloc(&d_cnt, n * 4)) != cudaSuccess || (e = cudaMalloc(&d_pool, batch_max * kPoolCap * 8)) != cudaSuccess ||
+        (e = cudaMalloc(&d_pcnt, batch_max * 4)) != cudaSuccess || (e = cudaMalloc(&d_vis, vis_warps * per_warp)) != cudaSuccess ||
+        (e = cudaMalloc(&d_rev, items * 4 * 5)) != cudaSuccess || (e = cudaMalloc(&d_sort, sort_bytes + 16)) != cudaSuccess ||
+        (e = cudaMalloc(&d_misc, 256)) != cudaSuccess) {
+        cleanup();
+        return cuda_fail(e, "graph builder buffers");
+    }
+    if ((e = cudaMemcpy(d_order, order.data(), n * 4, cudaMemcpyHostToDevice)) != cudaSuccess ||
+        (e = cudaMemset(d_cnt, 0, n * 4)) != cudaSuccess || (e = cudaMemset(d_vis, 0, vis_warps * per_warp)) != cudaSuccess ||
+        (e = cudaMemset(d_misc, 0, 256)) != cudaSuccess) {
+        cleanup();
+        return cuda_fail(e, "graph builder set-up");
+    }
+    a.order = static_cast<const uint32_t*>(d_order);
+    a.nbr_ids = ix->d_adj;
+    a.nbr_dist = static_cast<float*>(d_dist);
+    a.nbr_cnt = static_cast<uint32_t*>(d_cnt);
+    a.pool = static_cast<unsigned long long*>(d_pool);
+    a.pool_cnt = static_cast<uint32_t*>(d_pcnt);
+    a.pool_cap = kPoolCap;
+    a.vis = static_cast<uint32_t*>(d_vis);
+    a.vis_words = words;
+    a.vis_log_cap = kLogCap;
+    a.vis_warps = static_cast<uint32_t>(vis_warps);
+    uint32_t* rev = static_cast<uint32_t*>(d_rev);
+    a.seg_start = rev + 4 * items;
+    a.seg_count = static_cast<uint32_t*>(d_misc);
+    a.err = static_cast<unsigned int*>(d_misc) + 4;
+    // the batch loop (src/build_graph.cpp:303-369)
+    for (uint64_t start = 1; start < n;) {
+        const uint64_t end = std::min(std::min(start * 2, start + bound), n);
+        a.start = start;
+        a.count = end - start;
+        e = bsb::graph_build_batch(a, ix->smem_optin, ix->num_sms, d_sort, sort_bytes, rev, rev + items,
+                                   rev + 2 * items, rev + 3 * items, nullptr);
+        if (e != cudaSuccess) { cleanup(); return cuda_fail(e, "graph build batch"); }
+        start = end;
+    }
+    e = bsb::graph_build_finish(a, ix->smem_optin, ix->num_sms, nullptr);
+    unsigned int err = 0;
+    if (e == cudaSuccess) e = cudaMemcpy(&err, a.err, 4, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) { cleanup(); return cuda_fail(e, "graph build"); }
+    if (err) {
+        cleanup();
+        return fail(BS_ERR_KERNEL, "graph builder: %s (flags 0x%x)",
+                    (err & bsb::kErrPoolFull) ? "a build search expanded more than 2048 nodes"
+                                              : "a prune had more than 4096 candidates", err);
+    }
+    // missing slots are node 0 (src/build_graph.cpp:371): the tails past each count
+    {
+        std::vector<uint32_t> cnt(n);
+        if ((e = cudaMemcpy(cnt.data(), d_cnt, n * 4, cudaMemcpyDeviceToHost)) != cudaSuccess) { cleanup(); return cuda_fail(e, "graph counts"); }
+        std::vector<uint32_t> edges(n * deg);
+        if ((e = cudaMemcpy(edges.data(), ix->d_adj, n * deg * 4, cudaMemcpyDeviceToHost)) != cudaSuccess) { cleanup(); return cuda_fail(e, "graph edges"); }
+        for (uint64_t u = 0; u < n; ++u)
+            for (uint32_t j = cnt[u]; j < deg; ++j) edges[u * deg + j] = 0;
+        if ((e = cudaMemcpy(ix->d_adj, edges.data(), n * deg * 4, cudaMemcpyHostToDevice)) != cudaSuccess) { cleanup(); return cuda_fail(e, "graph edges"); }
+        if (edges_out) std::memcpy(edges_out, edges.data(), n * deg * 4);
+    }
+    cleanup();
+    // the layouts and the codebook that depended on the old graph
+    {
+        std::lock_guard<std::mutex> lk(ix->mu);
+        cudaFree(ix->d_nb);
+        ix->d_nb = nullptr;
+        ix->nb_tried = false;
+    }
+    cudaFree(ix->d_codes); cudaFree(ix->d_factors); cudaFree(ix->d_signs); cudaFree(ix->d_rqb);
+    ix->d_codes = nullptr; ix->d_factors = nullptr; ix->d_signs = nullptr; ix->d_rqb = nullptr;
+    ix->has_rabitq = false;
+    ix->rq_entry = BS_NO_NODE;
     return BS_OK;
 }
 

@@ -218,6 +218,42 @@ cudaError_t build_rabitq_blocks(const SearchParams& p, unsigned char* out, cudaS
 cudaError_t rabitq_grid_warps(const SearchParams& p, const LaunchShape& shape, int num_sms,
                               uint64_t& warps);
 
+// Vamana graph builder (bs_graph_build.cu): the reference build_graph's
+// batch loop on the GPU over the index's rows.
+struct GraphBuildArgs {
+    SearchParams sp;             // rows, dims, staging and distance-path fields (score_rows)
+    uint32_t degree;             // out-degree R
+    uint32_t L;                  // build beam width
+    float alpha;
+    const uint32_t* order;       // [n] insertion order (the reference's shuffle)
+    uint32_t* nbr_ids;           // [n][degree] current lists
+    float* nbr_dist;             // [n][degree] their stored distances
+    uint32_t* nbr_cnt;           // [n] list lengths
+    uint64_t start, count;       // batch: order[start, start + count)
+    unsigned long long* pool;    // [count][pool_cap] expanded (ord(dist) << 32 | node), expansion order
+    uint32_t* pool_cnt;          // [count]
+    uint32_t pool_cap;
+    uint32_t* vis;               // per warp: bitmap over the nodes, then a log
+    uint32_t vis_words, vis_log_cap, vis_warps;
+    // reverse edges of the batch, sorted by destination (stable)
+    const uint32_t* rev_dst;     // [count * degree], 0xffffffff past the valid ones
+    const uint32_t* rev_t;       // slot * degree + position in the slot's list
+    uint32_t* seg_start;         // segment starts in the sorted arrays
+    uint32_t* seg_count;         // [1] number of segments
+    uint32_t prune_cap;          // candidates a prune holds (shared memory)
+    unsigned int* err;           // error bits (kErrPoolFull, kErrPruneFull)
+};
+constexpr unsigned kErrPoolFull = 16u;    // a build search expanded more than pool_cap nodes
+constexpr unsigned kErrPruneFull = 32u;   // a prune had more than prune_cap candidates
+
+cudaError_t plan_graph_build(GraphBuildArgs& a, size_t smem_optin);
+cudaError_t graph_build_batch(GraphBuildArgs& a, size_t smem_optin, int num_sms, void* sort_tmp, size_t sort_tmp_bytes,
+                              uint32_t* rev_keys_in, uint32_t* rev_vals_in, uint32_t* rev_keys_out,
+                              uint32_t* rev_vals_out, cudaStream_t stream);
+cudaError_t graph_build_finish(GraphBuildArgs& a, size_t smem_optin, int num_sms, cudaStream_t stream);
+size_t graph_build_sort_bytes(uint64_t items);
+uint32_t graph_build_search_warps(const GraphBuildArgs& a, int num_sms, size_t smem_optin);
+
 // Merge of per-shard result lists (bs_merge.cu).
 constexpr uint32_t kMaxShards = 32;
 struct MergeArgs {

@@ -50,7 +50,8 @@ typedef struct bs_graph_desc {
     int32_t dim;
     int32_t degree;
     const float* vectors;     /* [num_nodes][dim]    */
-    const uint32_t* edges;    /* [num_nodes][degree] */
+    const uint32_t* edges;    /* [num_nodes][degree]; NULL: no graph yet (for
+                                 bs_index_build_graph)                        */
 } bs_graph_desc;
 
 /* Host-resident RaBitQ data (CPURabitqData, reference include/rabitq.hpp:25-35).
@@ -124,6 +125,24 @@ BS_API bs_status bs_index_build_codebook(bs_index* index, uint32_t seed, const c
 
 BS_API bs_status bs_index_info(const bs_index* index, uint64_t* num_nodes, int32_t* dim,
                                int32_t* degree);
+
+/* Parameters of the graph builder (the reference build_graph's options,
+ * src/build_graph.cpp:22-31; --metric ip is not supported). */
+typedef struct bs_graph_build_params {
+    int32_t beam_width;       /* build beam width L (reference default 128)  */
+    float alpha;              /* pruning alpha >= 1 (reference default 2.0)  */
+    uint32_t seed;            /* insertion-order shuffle seed (default 1234) */
+} bs_graph_build_params;
+
+/* Replaces the reference Vamana builder build_graph (src/build_graph.cpp:
+ * 255-397), on the GPU over the index's own rows: the same insertion order
+ * (std::mt19937(seed) + std::shuffle from the same standard library), batch
+ * schedule, greedy searches, robust prune and reverse edges, so the result is
+ * the reference's graph.bin.  The index's degree is the out-degree R (<= 64);
+ * create the index with edges == NULL.  The new adjacency replaces the
+ * index's; a codebook and the neighbourhood blocks built for the old one are
+ * dropped.  edges_out (host, nullable) receives [num_nodes][degree]. */
+BS_API bs_status bs_index_build_graph(bs_index* index, const bs_graph_build_params* params, uint32_t* edges_out);
 
 /* Replaces compute_entry_point (src/gpu_cli.cu:55-83): row nearest to the
  * float centroid, same arithmetic, computed on the GPU and cached. */
