@@ -288,10 +288,17 @@ cudaError_t plan_search(SearchParams& p, LaunchShape& shape, size_t max_smem_opt
         // With neighbourhood blocks the table only holds ids that passed
         // into the beam, so it is sized to the beam instead of
         // filter_capacity (more resident warps).
-        const uint64_t want = p.nb != nullptr ? 4ull * (p.topk + p.degree) : (p.filter_slots > need ? p.filter_slots : need);
+#ifndef BS_NB_TABLE_FACTOR
+#define BS_NB_TABLE_FACTOR 4     // block-layout table: slots >= factor * (topk + degree)
+#endif
+#ifndef BS_NB_TABLE_LOAD
+#define BS_NB_TABLE_LOAD 4       // ... rebuilt from the beam at 1/load of its slots
+#endif
+        const uint64_t want = p.nb != nullptr ? BS_NB_TABLE_FACTOR * (static_cast<uint64_t>(p.topk) + p.degree)
+                                              : (p.filter_slots > need ? p.filter_slots : need);
         const uint32_t slots = pow2_at_least(want);
         p.filter_slots = slots < 64 ? 64 : slots;
-        p.filter_limit = p.nb != nullptr ? p.filter_slots / 4u : p.filter_slots / 4u * 3u;
+        p.filter_limit = p.nb != nullptr ? p.filter_slots / BS_NB_TABLE_LOAD : p.filter_slots / 4u * 3u;
         p.filter_words = p.filter_slots;
     } else {
         const uint32_t bits = pow2_at_least(p.filter_slots < 32 ? 32 : p.filter_slots);

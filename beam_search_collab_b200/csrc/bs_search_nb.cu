@@ -157,7 +157,11 @@ __device__ __forceinline__ void score_direct(const SearchParams& p, uint32_t m, 
 }
 
 template <int RX, int RY, int DM, int FM>
+#ifdef BS_NB_MAXNREG
+__global__ void __maxnreg__(BS_NB_MAXNREG) k_search_nb(const SearchParams p) {
+#else
 __global__ void __launch_bounds__(256) k_search_nb(const SearchParams p) {
+#endif
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const unsigned lane = threadIdx.x & 31u;
     unsigned char* ws = smem_raw + static_cast<size_t>(threadIdx.x >> 5) * p.smem_per_warp;
