@@ -29,6 +29,8 @@ Arms
 --measure codebook times the GPU RaBitQ codebook builder on the workload's
 base and graph instead (one JSON line, edges/s; the reference build_rabitq on
 all host threads as the CPU baseline, and the two codebook files compared).
+--measure graph times the GPU graph builder on the workload's base (nodes/s)
+and compares its graph.bin with the reference build_graph's.
 
 Multi-GPU (torchrun, one rank per GPU): query sharding over a replicated
 index, no collective on the data path.  --scaling weak (default): every rank
@@ -750,6 +752,77 @@ def measure_codebook(args):
     }
 
 
+def measure_graph(args):
+    """--measure graph: the GPU graph builder (bs_index_build_graph) over the
+    workload's base, against the graph the reference build_graph wrote for it
+    (bench_data/<config>/graph.bin, --degree 32 --beam-width 128 --alpha 2.0
+    --seed 1234).  value = inserted nodes per second, device time of the whole
+    build (CUDA events; the upload is outside); e2e = the drop-in CLI
+    bin/build_graph end to end (read the fvecs, upload, build, write
+    graph.bin), wall clock; cpu_baseline = the reference build_graph on the
+    same file with all host threads, wall clock (skipped with
+    --no-cpu-baseline); `identical` = the files compared byte for byte."""
+    import filecmp
+    import torch
+    import beam_search_collab_b200 as B
+    from beam_search_collab_b200 import datasets as ds
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    cfg = CONFIGS[CFG_NAME]
+    s = getattr(ds, cfg["gen"])(nq=1, **cfg.get("gen_kwargs", {}))
+    ref_graph = os.path.join(DATA_DIR, cfg.get("data_dir", CFG_NAME), "graph.bin")
+    ref_edges = ds.read_graph(ref_graph)
+    degree = ref_edges.shape[1]
+    times, same = [], None
+    for i in range(max(1, args.steps)):
+        ix = B.Index.from_vectors(s.base, degree)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        edges = ix.build_graph(beam_width=128, alpha=2.0, seed=1234)
+        b.record()
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b))
+        ix.close()
+        rows_same = (edges == ref_edges).all(axis=1)
+        same = int(rows_same.sum()) if same is None else min(same, int(rows_same.sum()))
+    ms = statistics.median(times)
+    n = s.base.shape[0]
+    with tempfile.TemporaryDirectory() as tmp:
+        bp, gp, rp = os.path.join(tmp, "base.fvecs"), os.path.join(tmp, "ours.bin"), os.path.join(tmp, "ref.bin")
+        ds.write_fvecs(bp, s.base)
+        t = time.perf_counter()
+        subprocess.run([os.path.join(ROOT, "beam_search_collab_b200", "bin", "build_graph"), "--base", bp, "--graph", gp,
+                        "--degree", str(degree), "--beam-width", "128", "--alpha", "2.0", "--seed", "1234"],
+                       check=True, stdout=subprocess.DEVNULL)
+        e2e_s = time.perf_counter() - t
+        identical = filecmp.cmp(gp, ref_graph, shallow=False)
+        ref_s = None
+        tool = O.ref_tool("build_graph")
+        if tool is not None and not args.no_cpu_baseline:
+            t = time.perf_counter()
+            subprocess.run([tool, "--base", bp, "--graph", rp, "--degree", str(degree), "--beam-width", "128",
+                            "--alpha", "2.0", "--seed", "1234"], check=True, stdout=subprocess.DEVNULL,
+                           env=dict(os.environ, OMP_NUM_THREADS=str(host_threads())))
+            ref_s = time.perf_counter() - t
+    return {
+        "metric": "graph_build_nodes_per_s", "value": round(n / (ms / 1e3)), "unit": "nodes/s",
+        "n_gpus": 1, "steps": len(times), "warmup": 0, "ms_per_step": round(ms, 2),
+        "higher_is_better": True, "scaling": "none", "vs_baseline": None, "dtype": "u8" if s.base.max() <= 255 and
+        np.array_equal(s.base, np.rint(s.base)) and s.base.min() >= 0 else "f32",
+        "data": cfg["data"],
+        "config": {"workload": f"Vamana graph of {CFG_NAME}: {n} x {s.base.shape[1]}, degree {degree}, beam 128, "
+                               "alpha 2.0, seed 1234", "rows_identical_to_reference": same, "rows": n},
+        "e2e": {"value": round(n / e2e_s), "unit": "nodes/s", "seconds": round(e2e_s, 2),
+                "h2d_bytes_per_step": int(s.base.nbytes), "d2h_bytes_per_step": int(ref_edges.nbytes)},
+        "cpu_baseline": {"value": round(n / ref_s) if ref_s else None, "unit": "nodes/s",
+                         "seconds": round(ref_s, 2) if ref_s else None, "cores": host_threads(), "kind": "reference",
+                         "sample": "the whole build, reference build_graph (oracle/_ref) under OpenMP on all host "
+                                   "threads, wall clock incl. its file read and write"},
+        "identical": identical,
+    }
+
+
 # -------------------------------------------------------------------- main
 
 def main():
@@ -768,8 +841,8 @@ def main():
     ap.add_argument("--scaling", choices=("weak", "strong"), default="weak",
                     help="weak: every GPU searches its own 10,000 queries; strong: the workload's 10,000 "
                          "queries split over the GPUs")
-    ap.add_argument("--measure", choices=("search", "codebook"), default="search",
-                    help="codebook: time the GPU codebook builder instead of the search")
+    ap.add_argument("--measure", choices=("search", "codebook", "graph"), default="search",
+                    help="codebook / graph: time the GPU codebook or graph builder instead of the search")
     ap.add_argument("--profile-run", action="store_true",
                     help="for ncu: build the index, run `--warmup` searches and one more, print nothing else")
     args = ap.parse_args()
@@ -784,6 +857,8 @@ def main():
     args.warmup = max(args.warmup, 3)
     if args.measure == "codebook":
         return measure_codebook(args), 0
+    if args.measure == "graph":
+        return measure_graph(args), 0
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
