@@ -13,6 +13,9 @@ configuration stand in for them:
           x = normalize(20*mu + N(0, I)).
 * ``c4``  1,000,000 x 960 base, 1,000 queries: |N(0,1)| * 0.1 * s_j with a
           per-dimension scale s_j log-uniform in [0.1, 10].
+* ``c5``  8 shards of 12,500,000 x 128 (100M rows), 100,000 queries: integer
+          values in [0,255] from a mixture of 4,096 Gaussians; each shard is
+          drawn on its own (gen_c5_shard) by the rank that holds it.
 
 Every generator takes ``n``/``nq`` overrides so that tests can draw small
 samples with the same distributions.  Data seed = 1000 + config index, query
@@ -122,6 +125,29 @@ def gen_c4(n: int = 1_000_000, nq: int = 1_000, dim: int = 960) -> SyntheticSet:
         return out
 
     return SyntheticSet("c4", draw(_rng(seed + 10), n), draw(_rng(seed + 1), nq))
+
+
+def gen_c5_shard(shard: int, shard_rows: int = 12_500_000, nq: int = 100_000, dim: int = 128) -> SyntheticSet:
+    """Shard `shard` of the C5 base: integer values in [0,255] from a mixture of
+    4,096 Gaussians (as C2, more centres), rows shard*shard_rows ... of the
+    global base, drawn from the shard's own stream so that every rank makes only
+    its own rows; the queries are the same for every shard."""
+    seed = 1000 + 5
+    rc = _rng(seed)
+    centres = rc.uniform(-90.0, 200.0, size=(4096, dim)).astype(np.float32)
+
+    def draw(rng, m):
+        out = np.empty((m, dim), dtype=np.float32)
+        step = 1 << 17
+        for s in range(0, m, step):
+            e = min(m, s + step)
+            x = _mixture(rng, e - s, centres, 25.0)
+            np.rint(x, out=x)
+            np.clip(x, 0.0, 255.0, out=x)
+            out[s:e] = x
+        return out
+
+    return SyntheticSet(f"c5s{shard}", draw(_rng(seed + 100 + shard), shard_rows), draw(_rng(seed + 1), nq))
 
 
 GENERATORS = {"c1": gen_c1, "c2": gen_c2, "c3": gen_c3, "c4": gen_c4}

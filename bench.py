@@ -244,16 +244,18 @@ def load_graph():
     return ds.read_graph(GRAPH_C2)
 
 
-def gpu_ground_truth(base_t, q_t, k):
+def gpu_ground_truth(base_t, q_t, k, chunk=None):
     """Exact top-k ids by squared L2, ties by id (float64 on the GPU: exact for
-    these integer-valued vectors)."""
+    these integer-valued vectors).  `chunk` queries at a time (default: a
+    [chunk, n] float64 block of about 4 GB)."""
     import torch
     b64 = base_t.double()
     bn = (b64 * b64).sum(1)
     out = np.empty((q_t.shape[0], k), dtype=np.int64)
     extra = 32
-    for s in range(0, q_t.shape[0], 512):
-        q = q_t[s:s + 512].double()
+    chunk = chunk or max(1, min(512, (4 << 30) // (8 * base_t.shape[0])))
+    for s in range(0, q_t.shape[0], chunk):
+        q = q_t[s:s + chunk].double()
         d = bn[None, :] - 2.0 * (q @ b64.T) + (q * q).sum(1, keepdim=True)
         vals, idx = torch.topk(d, k + extra, dim=1, largest=False, sorted=True)
         vals, idx = vals.cpu().numpy(), idx.cpu().numpy()
@@ -752,6 +754,166 @@ def measure_codebook(args):
     }
 
 
+def run_sharded(args, rank, world, local_rank):
+    """--sharded: the C5 shape.  The index is cut into `world` shards of
+    --shard-rows rows (C5: 8 x 12,500,000 of a 100M-row base), one per GPU;
+    each rank draws its own rows, builds its shard's graph (GPU graph builder,
+    the reference build_graph's algorithm and file) and RaBitQ codebook (GPU
+    build_rabitq, seed 12345) on its own GPU.  A step searches every query on
+    every shard (rabitq, K 10, topk 256), all-gathers the shards' lists over
+    NCCL and merges them on the GPU into global ids (bs_merge_shards); value =
+    queries / max-over-ranks step time.  Checks: the merged rows against the
+    merge of the reference's own CPU search run on every shard's files (a
+    sample), and recall@10 against the exact top-10 over all shards."""
+    import torch
+    import torch.distributed as dist
+    import beam_search_collab_b200 as B
+    from beam_search_collab_b200 import datasets as ds
+    from beam_search_collab_b200.sharded import gather_shard_results
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    rows, nq, K_, topk = args.shard_rows, args.sharded_nq, 10, args.topk or 256
+    t0 = time.time()
+    s = ds.gen_c5_shard(rank, rows, nq)
+    t_data = time.time() - t0
+    ix = B.Index.from_vectors(s.base, 32, device=local_rank)
+    torch.cuda.synchronize()
+    t0 = time.time()
+    edges = ix.build_graph(beam_width=128, alpha=2.0, seed=1234)
+    t_graph = time.time() - t0
+    t0 = time.time()
+    entry = ix.build_codebook(12345)
+    t_cb = time.time() - t0
+    log(f"[rank {rank}] shard of {rows} rows: data {t_data:.1f}s, graph {t_graph:.1f}s, codebook {t_cb:.2f}s")
+    offsets = [r * rows for r in range(world)]
+    q = torch.from_numpy(s.queries).to(dev)
+    params = B.SearchParams(mode="rabitq", K=K_, topk_size=topk)
+    ids = torch.empty((nq, K_), dtype=torch.int32, device=dev)
+    dists = torch.empty((nq, K_), dtype=torch.float32, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+
+    def step():
+        ix.search_raw(q.data_ptr(), nq, ids.data_ptr(), dists.data_ptr(), params, stream=stream.cuda_stream)
+        with torch.cuda.stream(stream):
+            if world > 1:
+                ids_all, d_all = gather_shard_results(ids, dists)
+            else:
+                ids_all, d_all = ids.unsqueeze(0).contiguous(), dists.unsqueeze(0).contiguous()
+            return B.merge_shards(d_all, ids_all, offsets, K_, stream=stream.cuda_stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    with ClockSampler(local_rank) as clk:
+        for i in range(args.steps):
+            ev[i][0].record(stream)
+            out_ids, out_d = step()
+            ev[i][1].record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
+    errs = ix.take_errors(stream.cuda_stream)
+    # the search alone (its share of the step)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    ix.search_raw(q.data_ptr(), nq, ids.data_ptr(), dists.data_ptr(), params, stream=stream.cuda_stream)
+    b.record(stream)
+    torch.cuda.synchronize()
+    search_ms = a.elapsed_time(b)
+    t = torch.tensor([ms, search_ms, float(errs)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, search_ms, errs = float(t[0]), float(t[1]), int(t[2])
+    if errs:
+        raise SystemExit(f"search kernels reported error flags {errs:#x}")
+    merged = out_ids.cpu().numpy().view(np.uint32)
+
+    # exact top-10 over all shards for a sample (each rank its shard's top-10, merged)
+    ns = min(args.cpu_sample, nq)
+    base_t = torch.from_numpy(s.base).to(dev)
+    gt_local = gpu_ground_truth(base_t, q[:ns], 10)
+    del base_t
+    qs = s.queries[:ns].astype(np.float64)
+    gd = np.stack([((s.base[gt_local[i]].astype(np.float64) - qs[i]) ** 2).sum(1) for i in range(ns)])
+    gi = torch.from_numpy((gt_local + offsets[rank]).astype(np.int64)).to(dev)
+    gdt = torch.from_numpy(gd).to(dev)
+    if world > 1:
+        gi_all = [torch.empty_like(gi) for _ in range(world)]
+        gd_all = [torch.empty_like(gdt) for _ in range(world)]
+        dist.all_gather(gi_all, gi)
+        dist.all_gather(gd_all, gdt)
+        gi_all = torch.cat(gi_all, 1).cpu().numpy()
+        gd_all = torch.cat(gd_all, 1).cpu().numpy()
+    else:
+        gi_all, gd_all = gi.cpu().numpy(), gdt.cpu().numpy()
+    gt = np.stack([gi_all[i][np.lexsort((gi_all[i], gd_all[i]))][:10] for i in range(ns)])
+    recall = recall_at_k(merged[:ns].astype(np.int64), gt)
+
+    # parity: the reference CPU search on this shard's files, then the same merge
+    parity = None
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    # (the reference tools need the shard's base, graph and codebook as files:
+    # about 5 GB a million rows, so only for shards of up to 2M rows)
+    if O.ref_tool("ref_search_omp") is not None and not args.no_cpu_baseline and rows <= 2_000_000:
+        with tempfile.TemporaryDirectory() as tmp:
+            bp, qp, gp, cp = (os.path.join(tmp, f) for f in ("b.fvecs", "q.fvecs", "g.bin", "cb.bin"))
+            ds.write_fvecs(bp, s.base)
+            ds.write_fvecs(qp, s.queries[:ns])
+            with open(gp, "wb") as f:
+                np.array([rows, 32], dtype=np.int32).tofile(f)
+                edges.tofile(f)
+            ix.build_codebook(12345, cp)
+            info, ref_local = O.run_ref_search(gp, bp, qp, K=K_, topk=topk, mode="rabitq", codebook=cp,
+                                               threads=host_threads(), nq=ns, out=os.path.join(tmp, "ids.u32"))
+        rd = np.full(ref_local.shape, np.inf)
+        for i in range(ns):
+            ok = ref_local[i] != 0xFFFFFFFF
+            rd[i, ok] = ((s.base[ref_local[i][ok]].astype(np.float64) - qs[i]) ** 2).sum(1)
+        rg = np.where(ref_local != 0xFFFFFFFF, ref_local.astype(np.int64) + offsets[rank], -1)
+        rgt, rdt = torch.from_numpy(rg).to(dev), torch.from_numpy(rd).to(dev)
+        if world > 1:
+            ra = [torch.empty_like(rgt) for _ in range(world)]
+            rda = [torch.empty_like(rdt) for _ in range(world)]
+            dist.all_gather(ra, rgt)
+            dist.all_gather(rda, rdt)
+            ra, rda = torch.cat(ra, 1).cpu().numpy(), torch.cat(rda, 1).cpu().numpy()
+        else:
+            ra, rda = rgt.cpu().numpy(), rdt.cpu().numpy()
+        ref_merged = np.stack([ra[i][np.lexsort((ra[i], rda[i]))][:K_] for i in range(ns)])
+        same = (merged[:ns].astype(np.int64) == ref_merged).all(axis=1)
+        parity = {"queries": ns, "identical_rows": round(float(same.mean()), 6),
+                  "ids_match_frac": round(float((merged[:ns].astype(np.int64) == ref_merged).mean()), 6),
+                  "recall@10_reference": round(recall_at_k(ref_merged, gt), 5),
+                  "against": "the reference's own CPU RaBitQ search (oracle/_ref/ref_search_omp) on every shard's "
+                             "graph and codebook files, merged by (distance, global id)"}
+    if rank != 0:
+        return None
+    return {
+        "metric": "QPS (C5 sharded index, every query on every shard)",
+        "value": round(nq / (ms / 1e3), 1), "unit": "queries/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+        "scaling": "weak (index rows per GPU fixed)", "vs_baseline": None, "dtype": "u8",
+        "data": "synthetic: seeded C5 mixture (4,096 Gaussians, ints 0..255), each shard drawn by its rank; graphs "
+                "and codebooks built on the GPUs with the reference algorithms",
+        "config": {"workload": f"C5 shape: {world} shard(s) x {rows} rows x 128, {nq} queries, rabitq K {K_} "
+                               f"topk {topk}, NCCL all-gather + GPU merge",
+                   "index_rows": world * rows, "recall@10": round(recall, 5), "recall_sample": ns,
+                   "search_ms_max_rank": round(search_ms, 4),
+                   "exchange_and_merge_share": round(max(0.0, ms - search_ms) / ms, 4),
+                   "graph_build_s_rank0": round(t_graph, 2), "codebook_build_s_rank0": round(t_cb, 3),
+                   "parallelism": f"index-sharded over {world} GPU(s)"},
+        "parity": parity,
+        "gpu_launches": args.steps * 2,
+        "clocks": clk.summary(),
+    }
+
+
 def measure_graph(args):
     """--measure graph: the GPU graph builder (bs_index_build_graph) over the
     workload's base, against the graph the reference build_graph wrote for it
@@ -838,6 +1000,10 @@ def main():
     ap.add_argument("--cpu-sample", type=int, default=2000)
     ap.add_argument("--ref-sample", type=int, default=1000)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--sharded", action="store_true",
+                    help="C5 shape: an index sharded over the GPUs (see run_sharded)")
+    ap.add_argument("--shard-rows", type=int, default=12_500_000)
+    ap.add_argument("--sharded-nq", type=int, default=100_000)
     ap.add_argument("--scaling", choices=("weak", "strong"), default="weak",
                     help="weak: every GPU searches its own 10,000 queries; strong: the workload's 10,000 "
                          "queries split over the GPUs")
@@ -871,6 +1037,8 @@ def main():
                                              device_id=torch.device("cuda", local_rank))
     if args.impl == "reference":
         line = run_reference(args, rank, world)
+    elif args.sharded:
+        line = run_sharded(args, rank, world, local_rank)
     else:
         line = run_ours(args, rank, world, local_rank)
     if world > 1 and args.impl == "ours":
