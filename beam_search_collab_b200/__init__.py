@@ -73,7 +73,7 @@ class Stats(ctypes.Structure):
 # Every symbol include/bsearch.h declares (checked by the CPU test suite).
 EXPORTS = ("bs_search_params_default", "bs_index_create", "bs_index_load", "bs_index_attach_rabitq",
            "bs_index_load_codebook", "bs_index_build_codebook", "bs_index_info", "bs_index_entry_point", "bs_index_rabitq_entry",
-           "bs_index_build_graph", "bs_index_prepare", "bs_index_take_errors", "bs_index_destroy", "bs_search", "bs_search_no_alloc", "bs_merge_shards", "bs_device_alloc",
+           "bs_index_build_graph", "bs_ground_truth", "bs_index_prepare", "bs_index_take_errors", "bs_index_destroy", "bs_search", "bs_search_no_alloc", "bs_merge_shards", "bs_device_alloc",
            "bs_device_free",
            "bs_copy_to_device",
            "bs_copy_to_host", "bs_device_fill", "bs_synchronize", "bs_last_error", "bs_version")
@@ -104,6 +104,7 @@ def lib() -> ctypes.CDLL:
     L.bs_index_take_errors.argtypes = [vp, vp, _u32p]
     L.bs_index_prepare.argtypes = [vp, ctypes.c_char_p]
     L.bs_index_build_graph.argtypes = [vp, ctypes.POINTER(_BuildParams), _u32p]
+    L.bs_ground_truth.argtypes = [vp, vp, ctypes.c_uint32, ctypes.c_uint32, vp, vp, vp]
     L.bs_index_destroy.argtypes = [vp]
     L.bs_index_destroy.restype = None
     L.bs_search.argtypes = [vp, ctypes.POINTER(_Params), vp, ctypes.c_uint32, vp, vp,
@@ -121,7 +122,7 @@ def lib() -> ctypes.CDLL:
     L.bs_synchronize.argtypes = [vp, vp]
     for f in ("bs_index_create", "bs_index_load", "bs_index_attach_rabitq", "bs_index_load_codebook",
               "bs_index_build_codebook",
-              "bs_index_info", "bs_index_entry_point", "bs_index_rabitq_entry", "bs_index_take_errors", "bs_index_prepare", "bs_index_build_graph", "bs_search",
+              "bs_index_info", "bs_index_entry_point", "bs_index_rabitq_entry", "bs_index_take_errors", "bs_index_prepare", "bs_index_build_graph", "bs_ground_truth", "bs_search",
               "bs_device_alloc", "bs_device_free", "bs_copy_to_device", "bs_copy_to_host",
               "bs_device_fill", "bs_synchronize"):
         getattr(L, f).restype = st
@@ -253,6 +254,24 @@ class Index:
         e = ctypes.c_uint32()
         _check(lib().bs_index_entry_point(self._h, ctypes.byref(e)))
         return e.value
+
+    def ground_truth(self, queries, k: int, with_dists: bool = True, stream: int = 0):
+        """Exact k nearest rows of each query by brute force (bs_ground_truth):
+        (ids, dists) ordered by (distance, id); outputs live where the queries
+        live (numpy or a CUDA tensor)."""
+        if hasattr(queries, "data_ptr"):
+            import torch
+            nq = queries.shape[0]
+            ids = torch.empty((nq, k), dtype=torch.int32, device=queries.device)
+            dists = torch.empty((nq, k), dtype=torch.float32, device=queries.device) if with_dists else None
+        else:
+            queries = np.ascontiguousarray(queries, dtype=np.float32)
+            nq = queries.shape[0]
+            ids = np.empty((nq, k), dtype=np.uint32)
+            dists = np.empty((nq, k), dtype=np.float32) if with_dists else None
+        _check(lib().bs_ground_truth(self._h, ctypes.c_void_p(_ptr(queries)), nq, k, ctypes.c_void_p(_ptr(ids)),
+                                     ctypes.c_void_p(_ptr(dists) or None), ctypes.c_void_p(stream or None)))
+        return ids, dists
 
     def prepare(self, mode: str = "warp4") -> None:
         """Builds the device layout `mode` searches on (bs_index_prepare)."""

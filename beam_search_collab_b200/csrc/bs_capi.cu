@@ -976,6 +976,65 @@ BS_API bs_status bs_index_build_graph(bs_index* ix, const bs_graph_build_params*
     return BS_OK;
 }
 
+BS_API bs_status bs_ground_truth(bs_index* ix, const float* queries, uint32_t nq, uint32_t k, uint32_t* ids,
+                                 float* dists, void* stream_) {
+    if (!ix) return fail(BS_ERR_INVALID_ARGUMENT, "index is NULL");
+    if (k == 0 || k > 256) return fail(BS_ERR_UNSUPPORTED, "k must be in 1..256");
+    if (nq > 0 && (!queries || !ids)) return fail(BS_ERR_INVALID_ARGUMENT, "queries or ids is NULL");
+    if (nq == 0) return BS_OK;
+    DeviceGuard g(ix->device);
+    if (!g.ok) return fail(BS_ERR_CUDA, "cannot select device %d", ix->device);
+    if (any_foreign(ix->device, {queries, ids, dists}))
+        return fail(BS_ERR_INVALID_ARGUMENT, "a buffer lives on another GPU than the index (device %d)", ix->device);
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+    bsb::GroundTruthArgs a{};
+    {
+        ModeInfo mi{false, bsb::kHash, 4};
+        bs_search_params sp0;
+        bs_search_params_default(&sp0);
+        LaunchShape shape;
+        fill_params(ix, mi, &sp0, 0, a.sp, shape);
+        a.sp.nb = nullptr;
+    }
+    a.nq = nq;
+    a.k = k;
+    if (bsb::plan_ground_truth(a, ix->smem_optin, ix->num_sms) != cudaSuccess)
+        return fail(BS_ERR_UNSUPPORTED, "rows of %d dimensions do not fit the ground-truth kernel", ix->dim);
+    const bool q_dev = is_device_ptr(queries, ix->device);
+    const bool i_dev = is_device_ptr(ids, ix->device);
+    const bool d_dev = dists ? is_device_ptr(dists, ix->device) : true;
+    const size_t qbytes = static_cast<size_t>(nq) * ix->dim * 4, obytes = static_cast<size_t>(nq) * k * 4;
+    const size_t pbytes = static_cast<size_t>(a.splits) * nq * k * 4;
+    size_t off = 0;
+    const size_t q_off = off;
+    if (!q_dev) off += (qbytes + 255) & ~static_cast<size_t>(255);
+    const size_t i_off = off;
+    if (!i_dev) off += (obytes + 255) & ~static_cast<size_t>(255);
+    const size_t d_off = off;
+    if (dists && !d_dev) off += (obytes + 255) & ~static_cast<size_t>(255);
+    const size_t pd_off = off;
+    off += (pbytes + 255) & ~static_cast<size_t>(255);
+    const size_t pi_off = off;
+    off += (pbytes + 255) & ~static_cast<size_t>(255);
+    char* scratch = nullptr;
+    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&scratch), off, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "ground-truth scratch");
+    a.queries = q_dev ? queries : reinterpret_cast<const float*>(scratch + q_off);
+    a.out_ids = i_dev ? ids : reinterpret_cast<uint32_t*>(scratch + i_off);
+    a.out_dists = !dists ? nullptr : d_dev ? dists : reinterpret_cast<float*>(scratch + d_off);
+    a.part_d = reinterpret_cast<float*>(scratch + pd_off);
+    a.part_i = reinterpret_cast<uint32_t*>(scratch + pi_off);
+    if (!q_dev) e = cudaMemcpyAsync(scratch + q_off, queries, qbytes, cudaMemcpyHostToDevice, stream);
+    if (e == cudaSuccess) e = bsb::launch_ground_truth(a, ix->num_sms, stream);
+    if (e == cudaSuccess && !i_dev) e = cudaMemcpyAsync(ids, scratch + i_off, obytes, cudaMemcpyDeviceToHost, stream);
+    if (e == cudaSuccess && dists && !d_dev)
+        e = cudaMemcpyAsync(dists, scratch + d_off, obytes, cudaMemcpyDeviceToHost, stream);
+    cudaFreeAsync(scratch, stream);
+    if (e == cudaSuccess && (!q_dev || !i_dev || !d_dev)) e = cudaStreamSynchronize(stream);
+    if (e != cudaSuccess) return cuda_fail(e, "ground truth");
+    return BS_OK;
+}
+
 BS_API bs_status bs_index_prepare(bs_index* ix, const char* mode) {
     if (!ix) return fail(BS_ERR_INVALID_ARGUMENT, "index is NULL");
     ModeInfo mi;

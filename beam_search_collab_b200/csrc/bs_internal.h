@@ -254,6 +254,21 @@ cudaError_t graph_build_finish(GraphBuildArgs& a, size_t smem_optin, int num_sms
 size_t graph_build_sort_bytes(uint64_t items);
 uint32_t graph_build_search_warps(const GraphBuildArgs& a, int num_sms, size_t smem_optin);
 
+// Exact brute-force k nearest rows (bs_ground_truth.cu).
+struct GroundTruthArgs {
+    SearchParams sp;             // rows, dims, integer-exact range
+    const float* queries;        // [nq][dim] (device)
+    uint32_t nq, k, kcap;        // kcap: power of two >= k, >= 32
+    uint32_t splits;             // row ranges searched apart, then merged
+    uint32_t smem_per_warp, warps_per_block, off_qb, off_qq, off_lists;
+    float* part_d;               // [splits][nq][k]
+    uint32_t* part_i;
+    uint32_t* out_ids;           // [nq][k]
+    float* out_dists;            // [nq][k] or null
+};
+cudaError_t plan_ground_truth(GroundTruthArgs& a, size_t smem_optin, int num_sms);
+cudaError_t launch_ground_truth(const GroundTruthArgs& a, int num_sms, cudaStream_t stream);
+
 // Merge of per-shard result lists (bs_merge.cu).
 constexpr uint32_t kMaxShards = 32;
 struct MergeArgs {

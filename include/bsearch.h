@@ -152,6 +152,17 @@ BS_API bs_status bs_index_entry_point(bs_index* index, uint32_t* entry);
  * codebook is attached (reference src/gpu_cli.cu:436-437). */
 BS_API bs_status bs_index_rabitq_entry(const bs_index* index, uint32_t* entry);
 
+/* Replaces the ground-truth files the reference reads (src/gpu_cli.cu:379-381,
+ * made offline by script/unpack.py): the exact k nearest rows of every query
+ * by brute force over all the index's rows, ordered by (distance, id), with
+ * the search's own distances (the reference's sequential fp32 sums, or exact
+ * integer sums for byte rows and integer queries).  k <= 256.  queries
+ * [nq][dim], ids [nq][k] and dists [nq][k] (nullable) may be host or device
+ * pointers; with any host buffer the call returns when the results are in
+ * place, otherwise it is asynchronous on `stream`. */
+BS_API bs_status bs_ground_truth(bs_index* index, const float* queries, uint32_t nq, uint32_t k, uint32_t* ids,
+                                 float* dists, void* stream);
+
 /* No counterpart in the reference.  Builds the device layout the exact and
  * Bloom modes search fastest on (one contiguous neighbourhood block per node:
  * its adjacency row and its neighbours' rows, one bulk copy per expansion;
