@@ -10,6 +10,10 @@
 // Per call: a stream-ordered scratch block (counters, and staging for host
 // buffers) from cudaMallocAsync, released on the same stream.
 #include <cuda_runtime.h>
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
 
 #include <algorithm>
 #include <cmath>
@@ -509,6 +513,132 @@ void free_index(bs_index* ix) {
     delete ix;
 }
 
+// A file mapped read-only into the address space (the loaders stream it to
+// the device in chunks; the kernel pages it in as the chunks are copied).
+struct MappedFile {
+    int fd = -1;
+    const unsigned char* p = nullptr;
+    size_t size = 0;
+    ~MappedFile() {
+        if (p && size) munmap(const_cast<unsigned char*>(p), size);
+        if (fd >= 0) close(fd);
+    }
+    bool open_ro(const char* path) {
+        fd = ::open(path, O_RDONLY);
+        if (fd < 0) return false;
+        struct stat st;
+        if (fstat(fd, &st) != 0) return false;
+        size = static_cast<size_t>(st.st_size);
+        if (size == 0) return true;
+        void* m = mmap(nullptr, size, PROT_READ, MAP_PRIVATE, fd, 0);
+        if (m == MAP_FAILED) { size = 0; return false; }
+        madvise(m, size, MADV_SEQUENTIAL);
+        p = static_cast<const unsigned char*>(m);
+        return true;
+    }
+};
+
+// Streams `rows` rows of `in_row` bytes from host memory to the device in
+// chunks of about 64 MB through two page-locked buffers: while the GPU copies
+// and takes apart chunk c, the host reads chunk c + 1 from the mapping.  Each
+// chunk lands either at direct + first_row * in_row (a plain copy), or in a
+// device staging buffer handed to consume(chunk, first_row, rows, stream).
+template <class F>
+cudaError_t pipeline_rows(const unsigned char* src, uint64_t rows, uint64_t in_row, unsigned char* direct, F&& consume) {
+    if (rows == 0) return cudaSuccess;
+    const uint64_t per = std::max<uint64_t>(1, (64ull << 20) / in_row);
+    const uint64_t chunk = per * in_row;
+    void* pin[2] = {nullptr, nullptr};
+    void* dev[2] = {nullptr, nullptr};
+    cudaEvent_t ev[2] = {nullptr, nullptr};
+    cudaStream_t st = nullptr;
+    cudaError_t e = cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking);
+    for (int b = 0; b < 2 && e == cudaSuccess; ++b) {
+        e = cudaHostAlloc(&pin[b], chunk, cudaHostAllocDefault);
+        if (e == cudaSuccess && !direct) e = cudaMalloc(&dev[b], chunk);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ev[b], cudaEventDisableTiming);
+    }
+    for (uint64_t r0 = 0, c = 0; e == cudaSuccess && r0 < rows; r0 += per, ++c) {
+        const int b = static_cast<int>(c & 1u);
+        const uint64_t cnt = std::min(per, rows - r0);
+        if ((e = cudaEventSynchronize(ev[b])) != cudaSuccess) break;   // buffer b free again
+        std::memcpy(pin[b], src + r0 * in_row, cnt * in_row);
+        unsigned char* dst = direct ? direct + r0 * in_row : static_cast<unsigned char*>(dev[b]);
+        e = cudaMemcpyAsync(dst, pin[b], cnt * in_row, cudaMemcpyHostToDevice, st);
+        if (e == cudaSuccess && !direct) e = consume(static_cast<const uint32_t*>(dev[b]), r0, cnt, st);
+        if (e == cudaSuccess) e = cudaEventRecord(ev[b], st);
+    }
+    if (st) {
+        const cudaError_t s2 = cudaStreamSynchronize(st);
+        if (e == cudaSuccess) e = s2;
+        cudaStreamDestroy(st);
+    }
+    for (int b = 0; b < 2; ++b) {
+        if (pin[b]) cudaFreeHost(pin[b]);
+        if (dev[b]) cudaFree(dev[b]);
+        if (ev[b]) cudaEventDestroy(ev[b]);
+    }
+    return e;
+}
+
+float ord_to_float(uint32_t o) {
+    const uint32_t u = (o & 0x80000000u) ? (o & 0x7fffffffu) : ~o;
+    float f;
+    std::memcpy(&f, &u, 4);
+    return f;
+}
+
+// The index object with its device, dimensions, error word and an
+// adjacency array (not filled); the rows are the caller's to upload.
+bs_status create_index_shell(const bs_graph_desc* desc, int device, bs_index** out) {
+    *out = nullptr;
+    if (desc->num_nodes == 0 || desc->dim <= 0 || desc->degree <= 0)
+        return fail(BS_ERR_INVALID_ARGUMENT, "num_nodes, dim and degree must be positive");
+    if (desc->num_nodes >= (1ull << 31))
+        return fail(BS_ERR_UNSUPPORTED, "num_nodes must be below 2^31 (node ids are 31-bit)");
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
+        cudaGetLastError();
+        return fail(BS_ERR_CUDA, "no CUDA device available");
+    }
+    if (device < 0 || device >= ndev) return fail(BS_ERR_INVALID_ARGUMENT, "device %d out of range", device);
+    DeviceGuard g(device);
+    if (!g.ok) return fail(BS_ERR_CUDA, "cannot select device %d", device);
+    auto* ix = new (std::nothrow) bs_index();
+    if (!ix) return fail(BS_ERR_OUT_OF_MEMORY, "host allocation failed");
+    ix->device = device;
+    {
+        const char* env = std::getenv("BSEARCH_LAYOUT");
+        ix->gather_only = env && std::strcmp(env, "gather") == 0;
+    }
+    ix->n = desc->num_nodes;
+    ix->dim = desc->dim;
+    ix->degree = desc->degree;
+    ix->row_stride = (static_cast<uint32_t>(desc->dim) + 3u) & ~3u;
+    ix->row_bytes = (static_cast<uint32_t>(desc->dim) + 15u) & ~15u;
+    cudaDeviceProp prop;
+    cudaError_t e = cudaGetDeviceProperties(&prop, device);
+    if (e != cudaSuccess) { free_index(ix); return cuda_fail(e, "cudaGetDeviceProperties"); }
+    ix->num_sms = prop.multiProcessorCount;
+    ix->smem_optin = prop.sharedMemPerBlockOptin;
+    const size_t ebytes = static_cast<size_t>(ix->n) * ix->degree * sizeof(uint32_t);
+    if ((e = cudaMalloc(&ix->d_err, 256)) != cudaSuccess || (e = cudaMemset(ix->d_err, 0, 256)) != cudaSuccess) {
+        free_index(ix);
+        return cuda_fail(e, "error word");
+    }
+    if ((e = cudaMalloc(&ix->d_adj, ebytes)) != cudaSuccess) { free_index(ix); return cuda_fail(e, "adjacency"); }
+    // Per-call scratch comes from the device's stream-ordered pool: keep freed
+    // blocks cached instead of returning them at every synchronisation.
+    cudaMemPool_t pool;
+    if (cudaDeviceGetDefaultMemPool(&pool, device) == cudaSuccess) {
+        uint64_t keep = UINT64_MAX;
+        cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+    }
+    cudaGetLastError();
+    *out = ix;
+    return BS_OK;
+}
+
 bs_status ensure_entry(bs_index* ix) {
     std::lock_guard<std::mutex> lk(ix->mu);
     if (ix->entry_valid) return BS_OK;
@@ -550,36 +680,10 @@ BS_API bs_status bs_index_create(const bs_graph_desc* desc, int device, bs_index
     if (!out) return fail(BS_ERR_INVALID_ARGUMENT, "out is NULL");
     *out = nullptr;
     if (!desc || !desc->vectors) return fail(BS_ERR_INVALID_ARGUMENT, "graph descriptor or its vectors are NULL");
-    if (desc->num_nodes == 0 || desc->dim <= 0 || desc->degree <= 0)
-        return fail(BS_ERR_INVALID_ARGUMENT, "num_nodes, dim and degree must be positive");
-    if (desc->num_nodes >= (1ull << 31))
-        return fail(BS_ERR_UNSUPPORTED, "num_nodes must be below 2^31 (node ids are 31-bit)");
-    int ndev = 0;
-    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
-        cudaGetLastError();
-        return fail(BS_ERR_CUDA, "no CUDA device available");
-    }
-    if (device < 0 || device >= ndev) return fail(BS_ERR_INVALID_ARGUMENT, "device %d out of range", device);
-
+    bs_index* ix = nullptr;
+    bs_status s = create_index_shell(desc, device, &ix);
+    if (s != BS_OK) return s;
     DeviceGuard g(device);
-    if (!g.ok) return fail(BS_ERR_CUDA, "cannot select device %d", device);
-    auto* ix = new (std::nothrow) bs_index();
-    if (!ix) return fail(BS_ERR_OUT_OF_MEMORY, "host allocation failed");
-    ix->device = device;
-    {
-        const char* env = std::getenv("BSEARCH_LAYOUT");
-        ix->gather_only = env && std::strcmp(env, "gather") == 0;
-    }
-    ix->n = desc->num_nodes;
-    ix->dim = desc->dim;
-    ix->degree = desc->degree;
-    ix->row_stride = (static_cast<uint32_t>(desc->dim) + 3u) & ~3u;
-    cudaDeviceProp prop;
-    cudaError_t e = cudaGetDeviceProperties(&prop, device);
-    if (e != cudaSuccess) { free_index(ix); return cuda_fail(e, "cudaGetDeviceProperties"); }
-    ix->num_sms = prop.multiProcessorCount;
-    ix->smem_optin = prop.sharedMemPerBlockOptin;
-
     std::vector<uint64_t> neg_zeros;
     const uint64_t nvals = static_cast<uint64_t>(ix->n) * ix->dim;
     scan_values(desc->vectors, nvals, ix->int_exact, neg_zeros, ix->min_val, ix->max_val);
@@ -591,14 +695,8 @@ BS_API bs_status bs_index_create(const bs_graph_desc* desc, int device, bs_index
     ix->u8 = ix->int_exact && ix->min_val >= 0.0f && ix->max_val <= 255.0f && !storage_f32_forced() &&
              neg_zeros.size() <= nvals / 64;
     if (ix->u8) ix->neg_zeros.swap(neg_zeros);
-    ix->row_bytes = (static_cast<uint32_t>(desc->dim) + 15u) & ~15u;
-
     const size_t ebytes = static_cast<size_t>(ix->n) * ix->degree * sizeof(uint32_t);
-    if ((e = cudaMalloc(&ix->d_err, 256)) != cudaSuccess || (e = cudaMemset(ix->d_err, 0, 256)) != cudaSuccess) {
-        free_index(ix);
-        return cuda_fail(e, "error word");
-    }
-    if ((e = cudaMalloc(&ix->d_adj, ebytes)) != cudaSuccess) { free_index(ix); return cuda_fail(e, "adjacency"); }
+    cudaError_t e = cudaSuccess;
     if (ix->u8) {
         const size_t vbytes = static_cast<size_t>(ix->n) * ix->row_bytes;
         std::vector<uint8_t> packed;
@@ -629,32 +727,90 @@ BS_API bs_status bs_index_create(const bs_graph_desc* desc, int device, bs_index
     if (e == cudaSuccess)
         e = desc->edges ? cudaMemcpy(ix->d_adj, desc->edges, ebytes, cudaMemcpyHostToDevice) : cudaMemset(ix->d_adj, 0, ebytes);
     if (e != cudaSuccess) { free_index(ix); return cuda_fail(e, "index upload"); }
-    // Per-call scratch comes from the device's stream-ordered pool: keep freed
-    // blocks cached instead of returning them at every synchronisation.
-    cudaMemPool_t pool;
-    if (cudaDeviceGetDefaultMemPool(&pool, device) == cudaSuccess) {
-        uint64_t keep = UINT64_MAX;
-        cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
-    }
-    cudaGetLastError();
     *out = ix;
     return BS_OK;
 }
 
 BS_API bs_status bs_index_load(const char* graph_bin, const char* base_fvecs, int device, bs_index** out) {
+    if (!out) return fail(BS_ERR_INVALID_ARGUMENT, "out is NULL");
+    *out = nullptr;
     if (!graph_bin || !base_fvecs) return fail(BS_ERR_INVALID_ARGUMENT, "file path is NULL");
-    uint64_t n = 0, nv = 0;
-    int32_t deg = 0, dim = 0;
-    std::vector<uint32_t> edges;
-    std::vector<float> vecs;
-    std::string err;
-    if (!bsb::io::read_graph(graph_bin, n, deg, edges, err)) return fail(BS_ERR_IO, "%s", err.c_str());
-    if (!bsb::io::read_vecs<float>(base_fvecs, nv, dim, vecs, err)) return fail(BS_ERR_IO, "%s", err.c_str());
+    // both files checked before any device work (include/cpu_graph.hpp:125-173,
+    // include/data_loader.hpp:9-26 lay them out)
+    MappedFile gf, bf;
+    if (!gf.open_ro(graph_bin)) return fail(BS_ERR_IO, "Cannot open graph file: %s", graph_bin);
+    if (gf.size < 8) return fail(BS_ERR_IO, "Cannot read graph header: %s", graph_bin);
+    int32_t hdr[2];
+    std::memcpy(hdr, gf.p, 8);
+    if (hdr[0] <= 0 || hdr[1] <= 0) return fail(BS_ERR_IO, "Invalid graph header in: %s", graph_bin);
+    const uint64_t n = static_cast<uint64_t>(hdr[0]);
+    const int32_t deg = hdr[1];
+    if (gf.size < 8 + n * static_cast<uint64_t>(deg) * 4) return fail(BS_ERR_IO, "Truncated graph file: %s", graph_bin);
+    if (!bf.open_ro(base_fvecs)) return fail(BS_ERR_IO, "Cannot open %s", base_fvecs);
+    if (bf.size < 4) return fail(BS_ERR_IO, "Invalid vecs header in: %s", base_fvecs);
+    int32_t dim = 0;
+    std::memcpy(&dim, bf.p, 4);
+    if (dim <= 0) return fail(BS_ERR_IO, "Invalid vecs header in: %s", base_fvecs);
+    const uint64_t in_row = 4ull * (static_cast<uint64_t>(dim) + 1);
+    if (bf.size % in_row != 0) return fail(BS_ERR_IO, "Corrupt vecs file (size not a multiple of the row): %s", base_fvecs);
+    const uint64_t nv = bf.size / in_row;
     if (nv != n)
         return fail(BS_ERR_IO, "graph has %llu nodes but %s has %llu vectors", static_cast<unsigned long long>(n),
                     base_fvecs, static_cast<unsigned long long>(nv));
-    bs_graph_desc d{n, dim, deg, vecs.data(), edges.data()};
-    return bs_index_create(&d, device, out);
+    // the index's arrays, allocated empty, then filled from the mapped files
+    bs_graph_desc d{n, dim, deg, nullptr, nullptr};
+    bs_index* ix = nullptr;
+    bs_status s = create_index_shell(&d, device, &ix);
+    if (s != BS_OK) return s;
+    DeviceGuard g(device);
+    const uint64_t nvals = n * static_cast<uint64_t>(dim);
+    const size_t fbytes = static_cast<size_t>(n) * ix->row_stride * 4;
+    bsb::LoadScan h{};
+    h.all_int = 1;
+    h.min_ord = 0xffffffffu;
+    h.neg_zero_cap = nvals / 64 + 1;
+    bsb::LoadScan* d_scan = nullptr;
+    cudaError_t e = cudaMalloc(&ix->d_vecs, fbytes);
+    if (e == cudaSuccess) e = cudaMalloc(&d_scan, sizeof(bsb::LoadScan) + h.neg_zero_cap * 8);
+    if (e == cudaSuccess) {
+        h.neg_zero_pos = reinterpret_cast<unsigned long long*>(reinterpret_cast<char*>(d_scan) + sizeof(bsb::LoadScan));
+        e = cudaMemcpy(d_scan, &h, sizeof(h), cudaMemcpyHostToDevice);
+    }
+    // graph payload as it is; base rows taken apart and scanned on the GPU
+    if (e == cudaSuccess)
+        e = pipeline_rows(gf.p + 8, n, static_cast<uint64_t>(deg) * 4, reinterpret_cast<unsigned char*>(ix->d_adj),
+                          [](const uint32_t*, uint64_t, uint64_t, cudaStream_t) { return cudaSuccess; });
+    const uint32_t row_stride = ix->row_stride;
+    float* d_vecs = ix->d_vecs;
+    if (e == cudaSuccess)
+        e = pipeline_rows(bf.p, n, in_row, nullptr, [&](const uint32_t* raw, uint64_t r0, uint64_t cnt, cudaStream_t st) {
+            return bsb::load_fvecs_chunk(raw, cnt, r0, static_cast<uint32_t>(dim), row_stride, d_vecs, d_scan, st);
+        });
+    if (e == cudaSuccess) e = cudaMemcpy(&h, d_scan, sizeof(h), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) { cudaFree(d_scan); free_index(ix); return cuda_fail(e, "index upload"); }
+    if (h.bad_rows) { cudaFree(d_scan); free_index(ix); return fail(BS_ERR_IO, "Inconsistent row dimension in: %s", base_fvecs); }
+    ix->int_exact = h.all_int != 0;
+    ix->min_val = h.min_ord == 0xffffffffu ? 0.0f : ord_to_float(h.min_ord);
+    ix->max_val = h.max_ord == 0u ? 0.0f : ord_to_float(h.max_ord);
+    ix->u8 = ix->int_exact && ix->min_val >= 0.0f && ix->max_val <= 255.0f && !storage_f32_forced() &&
+             h.neg_zero_count <= nvals / 64;
+    if (ix->u8) {
+        // the exact byte copy replaces the f32 rows; the -0.0 positions are
+        // kept (ascending) for a codebook written from this index
+        ix->neg_zeros.resize(h.neg_zero_count);
+        if (h.neg_zero_count)
+            e = cudaMemcpy(ix->neg_zeros.data(), h.neg_zero_pos, h.neg_zero_count * 8, cudaMemcpyDeviceToHost);
+        std::sort(ix->neg_zeros.begin(), ix->neg_zeros.end());
+        if (e == cudaSuccess) e = cudaMalloc(&ix->d_vecs8, static_cast<size_t>(n) * ix->row_bytes);
+        if (e == cudaSuccess) e = bsb::rows_to_u8(ix->d_vecs, n, dim, ix->row_stride, ix->row_bytes, ix->d_vecs8, nullptr);
+        if (e == cudaSuccess) e = cudaDeviceSynchronize();
+        cudaFree(ix->d_vecs);
+        ix->d_vecs = nullptr;
+    }
+    cudaFree(d_scan);
+    if (e != cudaSuccess) { free_index(ix); return cuda_fail(e, "index upload"); }
+    *out = ix;
+    return BS_OK;
 }
 
 BS_API bs_status bs_index_attach_rabitq(bs_index* ix, const bs_rabitq_desc* d) {
@@ -693,11 +849,46 @@ BS_API bs_status bs_index_attach_rabitq(bs_index* ix, const bs_rabitq_desc* d) {
 
 BS_API bs_status bs_index_load_codebook(bs_index* ix, const char* path) {
     if (!ix || !path) return fail(BS_ERR_INVALID_ARGUMENT, "index or path is NULL");
-    bsb::io::Codebook cb;
-    std::string err;
-    if (!bsb::io::read_codebook(path, ix->n, ix->dim, ix->degree, cb, err)) return fail(BS_ERR_IO, "%s", err.c_str());
-    bs_rabitq_desc d{cb.entry, cb.padded_dim, cb.codes.data(), cb.factors.data(), cb.signs.data()};
-    return bs_index_attach_rabitq(ix, &d);
+    // codebook.bin (include/rabitq.hpp:49-97): u32 entry, n rows of
+    // [raw vector (dim) | codes (wpp*deg) | factors (3*deg) | neighbour ids
+    // (deg)] 4-byte slots, f32 signs[padded_dim]; the rows are streamed to the
+    // device and taken apart there
+    MappedFile f;
+    if (!f.open_ro(path)) return fail(BS_ERR_IO, "Cannot open codebook: %s", path);
+    const int32_t pdim = bsb::io::padded_dim_of(ix->dim);
+    if (pdim < 32) return fail(BS_ERR_UNSUPPORTED, "RaBitQ needs dim > 16 (padded_dim >= 32)");
+    const uint64_t wpp = static_cast<uint64_t>(pdim) / 32, deg = static_cast<uint64_t>(ix->degree);
+    const uint64_t row = static_cast<uint64_t>(ix->dim) + wpp * deg + 4 * deg;
+    if (f.size < 4 + ix->n * row * 4 + static_cast<uint64_t>(pdim) * 4)
+        return fail(BS_ERR_IO, "Truncated codebook (or dim/degree mismatch): %s", path);
+    uint32_t entry = 0;
+    std::memcpy(&entry, f.p, 4);
+    if (entry != BS_NO_NODE && entry >= ix->n)
+        return fail(BS_ERR_INVALID_ARGUMENT, "codebook entry point %u out of range", entry);
+    DeviceGuard g(ix->device);
+    cudaFree(ix->d_codes);
+    cudaFree(ix->d_factors);
+    cudaFree(ix->d_signs);
+    ix->d_codes = nullptr; ix->d_factors = nullptr; ix->d_signs = nullptr;
+    ix->has_rabitq = false;
+    cudaError_t e;
+    if ((e = cudaMalloc(&ix->d_codes, ix->n * deg * wpp * 4)) != cudaSuccess) return cuda_fail(e, "codes");
+    if ((e = cudaMalloc(&ix->d_factors, ix->n * 3 * deg * 4)) != cudaSuccess) return cuda_fail(e, "factors");
+    if ((e = cudaMalloc(&ix->d_signs, static_cast<size_t>(pdim) * 4)) != cudaSuccess) return cuda_fail(e, "signs");
+    uint32_t* codes = ix->d_codes;
+    float* factors = ix->d_factors;
+    const uint32_t dim = static_cast<uint32_t>(ix->dim), dg = static_cast<uint32_t>(deg), w = static_cast<uint32_t>(wpp);
+    e = pipeline_rows(f.p + 4, ix->n, row * 4, nullptr, [&](const uint32_t* raw, uint64_t r0, uint64_t cnt, cudaStream_t st) {
+        return bsb::load_codebook_chunk(raw, cnt, r0, dim, dg, w, codes, factors, st);
+    });
+    if (e == cudaSuccess)
+        e = cudaMemcpy(ix->d_signs, f.p + 4 + ix->n * row * 4, static_cast<size_t>(pdim) * 4, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return cuda_fail(e, "codebook upload");
+    ix->pdim = pdim;
+    ix->rq_entry = entry;
+    ix->has_rabitq = true;
+    if ((e = build_rq_blocks(ix)) != cudaSuccess) return cuda_fail(e, "rabitq node blocks");
+    return BS_OK;
 }
 
 BS_API bs_status bs_index_build_codebook(bs_index* ix, uint32_t seed, const char* out_path, uint32_t* entry_out) {

@@ -254,6 +254,22 @@ cudaError_t graph_build_finish(GraphBuildArgs& a, size_t smem_optin, int num_sms
 size_t graph_build_sort_bytes(uint64_t items);
 uint32_t graph_build_search_warps(const GraphBuildArgs& a, int num_sms, size_t smem_optin);
 
+// File loaders, device side (bs_load.cu).
+struct LoadScan {
+    unsigned int all_int;            // 1 until a value that is not an integer is seen
+    unsigned int bad_rows;           // 1: a row's header differs from the dimension
+    unsigned int min_ord, max_ord;   // ordered-int encodings of the smallest / largest value
+    unsigned long long neg_zero_count;
+    unsigned long long neg_zero_cap;
+    unsigned long long* neg_zero_pos;  // flat positions of -0.0 values (unordered)
+};
+cudaError_t load_fvecs_chunk(const uint32_t* raw, uint64_t rows, uint64_t first_row, uint32_t dim, uint32_t row_stride,
+                             float* out, LoadScan* scan, cudaStream_t stream);
+cudaError_t rows_to_u8(const float* in, uint64_t n, uint32_t dim, uint32_t row_stride, uint32_t row_bytes, uint8_t* out,
+                       cudaStream_t stream);
+cudaError_t load_codebook_chunk(const uint32_t* raw, uint64_t rows, uint64_t first_row, uint32_t dim, uint32_t deg,
+                                uint32_t wpp, uint32_t* codes, float* factors, cudaStream_t stream);
+
 // Exact brute-force k nearest rows (bs_ground_truth.cu).
 struct GroundTruthArgs {
     SearchParams sp;             // rows, dims, integer-exact range

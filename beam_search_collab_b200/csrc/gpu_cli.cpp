@@ -96,26 +96,22 @@ int main() {
         const std::string codebook_file = jd.value("codebook", std::string());
         const std::string results_file = jd.value("results", std::string());
 
-        // host copies (CPUGraph::load, include/cpu_graph.hpp:125-173)
-        uint64_t n = 0, nv = 0, nq = 0, ngt = 0;
+        // graph + base (CPUGraph::load + GPUGraph, include/cpu_graph.hpp:125-173):
+        // the files stream straight to the device (bs_index_load)
+        bs_index* index = nullptr;
+        if (bs_index_load(graph_file.c_str(), base_file.c_str(), 0, &index) != BS_OK) return die(bs_last_error());
+        uint64_t n = 0, nq = 0, ngt = 0;
         int32_t degree = 0, dim = 0, qdim = 0, gt_k = 0;
-        std::vector<uint32_t> edges;
-        std::vector<float> vecs, queries;
+        bs_index_info(index, &n, &dim, &degree);
+        std::cout << "Loaded graph: " << n << " nodes, degree " << degree << " from " << graph_file << "\n";
+        std::cout << "Loaded vectors: " << n << " x " << dim << " from " << base_file << "\n";
+        std::vector<float> queries;
         std::vector<int32_t> gt;
         std::string err;
-        if (!bsb::io::read_graph(graph_file, n, degree, edges, err)) return die(err);
-        std::cout << "Loaded graph: " << n << " nodes, degree " << degree << " from " << graph_file << "\n";
-        if (!bsb::io::read_vecs<float>(base_file, nv, dim, vecs, err)) return die(err);
-        if (nv != n) return die("base vector count does not match the graph");
-        std::cout << "Loaded vectors: " << n << " x " << dim << " from " << base_file << "\n";
         if (!bsb::io::read_vecs<float>(query_file, nq, qdim, queries, err)) return die(err);
         if (nq > 0 && qdim != dim) return die("query dimension does not match the base vectors");
         if (!bsb::io::read_vecs<int32_t>(gt_file, ngt, gt_k, gt, err)) return die(err);
         if (ngt < nq) return die("ground truth has fewer rows than queries");
-
-        bs_index* index = nullptr;
-        bs_graph_desc desc{n, dim, degree, vecs.data(), edges.data()};
-        if (!check(bs_index_create(&desc, 0, &index), "bs_index_create")) return 1;
         uint32_t entry = 0;
         if (!check(bs_index_entry_point(index, &entry), "bs_index_entry_point")) return 1;
 
