@@ -64,7 +64,7 @@ class Stats(ctypes.Structure):
                 ("estimates", ctypes.c_uint64), ("rerank", ctypes.c_uint64),
                 ("error_flags", ctypes.c_uint32), ("entry_point", ctypes.c_uint32),
                 ("integer_exact", ctypes.c_uint32), ("row_bytes", ctypes.c_uint32),
-                ("block_bytes", ctypes.c_uint32), ("reserved", ctypes.c_uint32)]
+                ("block_bytes", ctypes.c_uint32), ("warps_per_query", ctypes.c_uint32)]
 
     def as_dict(self):
         return {k: getattr(self, k) for k, _ in self._fields_}

@@ -29,7 +29,7 @@ CLI = os.path.join(BIN_DIR, "gpu_cli")
 RQ_CLI = os.path.join(BIN_DIR, "build_rabitq")
 BG_CLI = os.path.join(BIN_DIR, "build_graph")
 
-CU_SOURCES = ["bs_search.cu", "bs_search_nb.cu", "bs_rabitq.cu", "bs_rabitq_nb.cu", "bs_graph_build.cu", "bs_ground_truth.cu", "bs_load.cu", "bs_entry.cu", "bs_merge.cu", "bs_codebook.cu",
+CU_SOURCES = ["bs_search.cu", "bs_search_nb.cu", "bs_search_bq.cu", "bs_rabitq.cu", "bs_rabitq_nb.cu", "bs_graph_build.cu", "bs_ground_truth.cu", "bs_load.cu", "bs_entry.cu", "bs_merge.cu", "bs_codebook.cu",
               "bs_capi.cu"]
 NVCC_FLAGS = ["-std=c++17", "-O3", "-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo",
               "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",

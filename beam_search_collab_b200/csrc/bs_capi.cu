@@ -164,12 +164,13 @@ struct ModeInfo {
     bool rabitq = false;
     bsb::FilterMode fmode = bsb::kHash;
     int warps = 4;
+    bool block = false;     // base: one thread block per query (when the blocks fit)
 };
 
 bool parse_mode(const char* m, ModeInfo& mi) {
     if (!m) return false;
     const std::string s(m);
-    if (s == "base") { mi = {false, bsb::kHash, 4}; return true; }
+    if (s == "base") { mi = {false, bsb::kHash, 4, true}; return true; }
     if (s == "rabitq") { mi = {true, bsb::kHash, 4}; return true; }
     const struct { const char* name; bsb::FilterMode f; int w; } table[] = {
         {"warp1", bsb::kHash, 1},   {"warp2", bsb::kHash, 2},   {"warp4", bsb::kHash, 4},
@@ -422,6 +423,18 @@ cudaError_t plan(const bs_index* ix, SearchParams& p, LaunchShape& shape, char* 
         }
         p.rq_nb = nullptr;   // the gather kernel
     }
+    if (shape.block_query) {
+        // base: one thread block per query over the neighbourhood blocks;
+        // without them (blocks too large or off) the warp kernels below
+        SearchParams p1 = p;
+        LaunchShape s1 = shape;
+        if (p.nb != nullptr && bsb::plan_search_bq(p1, s1, ix->smem_optin, why, why_len) == cudaSuccess) {
+            p = p1;
+            shape = s1;
+            return cudaSuccess;
+        }
+        shape.block_query = 0;
+    }
     SearchParams p0 = p;
     const LaunchShape s0 = shape;
     const cudaError_t e = bsb::plan_search(p, shape, ix->smem_optin, why, why_len);
@@ -443,6 +456,7 @@ cudaError_t entry_kernels(const bs_index* ix, uint32_t* d_out, float* scratch, c
 void fill_params(const bs_index* ix, const ModeInfo& mi, const bs_search_params* prm, uint32_t entry,
                  SearchParams& p, LaunchShape& shape) {
     p = SearchParams{};
+    p.sm_count = static_cast<uint32_t>(ix->num_sms);
     p.vecs = ix->d_vecs;
     p.vecs8 = ix->d_vecs8;
     p.row_bytes = ix->row_bytes;
@@ -494,6 +508,7 @@ void fill_params(const bs_index* ix, const ModeInfo& mi, const bs_search_params*
     else shape.dmode = p.team_qlo <= p.team_qhi ? bsb::kTeam : bsb::kSeq;
     shape.fmode = mi.fmode;
     shape.warps_per_block = mi.warps;
+    shape.block_query = mi.block ? 1 : 0;
 }
 
 void free_index(bs_index* ix) {
@@ -1303,6 +1318,7 @@ BS_API bs_status bs_search(bs_index* ix, const bs_search_params* prm, const floa
         stats->integer_exact = use_team ? 1u : 0u;
         stats->row_bytes = ix->u8 ? ix->row_bytes : ix->row_stride * 4u;
         stats->block_bytes = p.nb ? p.nb_stride : p.rq_nb ? p.rq_stride : 0u;
+        stats->warps_per_query = shape.block_query ? static_cast<uint32_t>(shape.warps_per_block) : 1u;
     }
     if (nq == 0) return BS_OK;
 
@@ -1372,9 +1388,10 @@ BS_API bs_status bs_search(bs_index* ix, const bs_search_params* prm, const floa
         if (e == cudaSuccess) e = bsb::launch_search_rq_nb(p, shape, ix->num_sms, stream);
         if (e == cudaSuccess) e = cudaEventRecord(ix->rq_event, stream);
     } else {
-        e = mi.rabitq ? bsb::launch_search_rabitq(p, shape, ix->num_sms, stream)
-            : p.nb    ? bsb::launch_search_nb(p, shape, ix->num_sms, stream)
-                      : bsb::launch_search(p, shape, ix->num_sms, stream);
+        e = mi.rabitq          ? bsb::launch_search_rabitq(p, shape, ix->num_sms, stream)
+            : shape.block_query ? bsb::launch_search_bq(p, shape, ix->num_sms, stream)
+            : p.nb              ? bsb::launch_search_nb(p, shape, ix->num_sms, stream)
+                                : bsb::launch_search(p, shape, ix->num_sms, stream);
     }
     if (e != cudaSuccess) { release(); return cuda_fail(e, "search launch"); }
 
@@ -1528,8 +1545,9 @@ BS_API bs_status bs_search_no_alloc(bs_index* ix, const bs_search_params* prm, c
     // counters must start from zero
     cudaError_t e = cudaMemsetAsync(scratch, 0, sizeof(DevCounters), stream);
     if (e != cudaSuccess) return cuda_fail(e, "fixed scratch reset");
-    e = p.nb ? bsb::launch_search_nb(p, shape, ix->num_sms, stream)
-             : bsb::launch_search(p, shape, ix->num_sms, stream);
+    e = shape.block_query ? bsb::launch_search_bq(p, shape, ix->num_sms, stream)
+        : p.nb            ? bsb::launch_search_nb(p, shape, ix->num_sms, stream)
+                          : bsb::launch_search(p, shape, ix->num_sms, stream);
     if (e != cudaSuccess) return cuda_fail(e, "search launch");
     return BS_OK;
 }

@@ -537,7 +537,7 @@ cudaError_t plan_graph_build(GraphBuildArgs& a, size_t smem_optin) {
     if (!p.vecs8 && !(p.team_qlo <= p.team_qhi)) {
         const uint32_t row_bytes = p.stage_pitch * 4u;
         if (row_bytes > 1024u) {
-            p.stage_ring = 1;
+            p.stage_ring = dev::kRingStages;
             off = a16(off + dev::kRingFloats * 4u);
         } else {
             uint32_t rows = (24u * 1024u) / row_bytes;

@@ -113,7 +113,9 @@ struct SearchParams {
     // staging
     uint32_t stage_rows;        // rows staged per round in kSeq mode
     uint32_t stage_pitch;       // floats between staged rows (odd multiple of 4)
-    uint32_t stage_ring;        // kSeq wide rows: 1 = stream row chunks through a ring (bs_score.cuh)
+    uint32_t stage_ring;        // kSeq wide rows: chunks in the ring of row chunks (0: no ring; 4, 5, 6
+                                // or 8, bs_score.cuh)
+    uint32_t sm_count;          // the device's SMs (the planner sizes the ring so that nq warps stay resident)
     // per-warp shared-memory carve-up (bytes)
     uint32_t smem_per_warp;
     uint32_t off_q8;            // kU8: the query as packed u8 (row_bytes)
@@ -186,7 +188,14 @@ struct LaunchShape {
     FilterMode fmode;
     int warps_per_block;
     size_t smem_per_warp;
+    int block_query;            // 1: one thread block per query (mode base; bs_search_bq.cu)
 };
+
+// Bytes between the two block buffers of the block-per-query kernel.
+#ifdef __CUDACC__
+__host__ __device__
+#endif
+inline constexpr uint32_t bq_buffer_pitch(uint32_t nb_stride) { return (nb_stride + 127u) & ~127u; }
 
 // Host launchers implemented in bs_search.cu.  Return cudaSuccess or the
 // launch error; shape.smem_per_warp is filled by plan_search.
@@ -202,6 +211,14 @@ cudaError_t launch_search_rabitq(const SearchParams& p, const LaunchShape& shape
 // Neighbourhood-block variant of launch_search (p.nb set; bs_search_nb.cu).
 cudaError_t launch_search_nb(const SearchParams& p, const LaunchShape& shape, int num_sms,
                              cudaStream_t stream);
+// Block-per-query variant over the neighbourhood blocks (mode base;
+// bs_search_bq.cu): its own shared-memory carve-up (per block, in
+// shape.smem_per_warp) and launch.  BSEARCH_BQ_WARPS=2|4 fixes the warps per
+// query (default: 4 when the launch's queries fit the GPU at 8 blocks per
+// SM, else 2).
+cudaError_t plan_search_bq(SearchParams& p, LaunchShape& shape, size_t max_smem_optin, char* why,
+                           size_t why_len);
+cudaError_t launch_search_bq(const SearchParams& p, const LaunchShape& shape, int num_sms, cudaStream_t stream);
 // Builds the neighbourhood blocks from the gather layout (bs_search_nb.cu).
 cudaError_t build_neighbourhood_blocks(const SearchParams& p, unsigned char* out, cudaStream_t stream);
 

@@ -529,7 +529,7 @@ cudaError_t plan_search_rq_nb(SearchParams& p, LaunchShape& shape, size_t max_sm
     buf = buf > p.pdim * 5u ? buf : a16(p.pdim * 5u);           // rotated query + quantised bytes
     if (shape.dmode == kSeq) {
         if (p.row_stride * 4u > 1024u) {
-            p.stage_ring = 1;
+            p.stage_ring = kRingStages;
             p.stage_rows = 0;
             buf = buf > kRingFloats * 4u ? buf : kRingFloats * 4u;
         } else {

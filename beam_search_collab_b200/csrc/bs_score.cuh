@@ -54,48 +54,49 @@ __device__ __forceinline__ void score_rows_seq(const SearchParams& p, uint32_t m
 }
 
 // Wide rows (the 960-d C4 rows are 3.84 KB): the same sequential order, with
-// the rows streamed through a ring of kRingStages chunks of kRingCh
-// dimensions of up to 32 rows -- every lane folds its own row while the next
-// chunks are in flight -- so a warp holds kRingStages * 32 * kRingPitch
-// floats of shared memory instead of whole rows.  Each lane keeps its running
-// sum in a register across chunks and adds the elements d = 0..row_stride-1
-// in order with separately rounded operations: the reference's bits (the zero
-// pad of the stored rows and of the query adds +0).
+// the rows streamed through a ring of S chunks of kRingCh dimensions of up to
+// 32 rows -- every lane folds its own row while the next S-1 chunks are in
+// flight -- so a warp holds S * 32 * kRingPitch floats of shared memory
+// instead of whole rows.  Each lane keeps its running sum in a register
+// across chunks and adds the elements d = 0..row_stride-1 in order with
+// separately rounded operations: the reference's bits (the zero pad of the
+// stored rows and of the query adds +0).  S (p.stage_ring) is chosen by the
+// planner: the deepest ring that still keeps every query of the launch
+// resident (more bytes in flight per SM without a second wave).
 constexpr uint32_t kRingCh = 32;       // dimensions per chunk
-#ifndef BS_RING_STAGES
-#define BS_RING_STAGES 4
-#endif
-constexpr uint32_t kRingStages = BS_RING_STAGES;  // chunks in the ring (all but one in flight while one is folded)
+constexpr uint32_t kRingStages = 4;    // the default (and the builders') ring
 constexpr uint32_t kRingPitch = 36;    // floats per staged row chunk: 9 16-byte units, odd
-constexpr uint32_t kRingFloats = kRingStages * 32u * kRingPitch;
+constexpr uint32_t kRingStageFloats = 32u * kRingPitch;
+constexpr uint32_t kRingFloats = kRingStages * kRingStageFloats;
 
-__device__ __forceinline__ void score_rows_seq_ring(const SearchParams& p, uint32_t m, const uint32_t* cids,
-                                                    float* cdist, const float* qsm, float* ring,
-                                                    unsigned lane) {
+template <uint32_t S>
+__device__ __forceinline__ void score_rows_seq_ring_s(const SearchParams& p, uint32_t m, const uint32_t* cids,
+                                                      float* cdist, const float* qsm, float* ring,
+                                                      unsigned lane) {
     const uint32_t nch = (p.row_stride + kRingCh - 1) / kRingCh;
     const uint32_t part = lane & 7u;     // 16-byte piece of a row chunk this lane copies
     for (uint32_t g0 = 0; g0 < m; g0 += 32) {
         const uint32_t rows = min(32u, m - g0);
         // one commit group per chunk (empty past the last one), so that
-        // wait_group kRingStages-1 always means "chunk c has landed"
+        // wait_group S-1 always means "chunk c has landed"
         auto issue = [&](uint32_t c) {
             if (c < nch) {
                 const uint32_t d = c * kRingCh + part * 4u;
-                float* st = ring + (c % kRingStages) * 32u * kRingPitch + part * 4u;
+                float* st = ring + (c % S) * kRingStageFloats + part * 4u;
                 if (d < p.row_stride)
                     for (uint32_t r = lane >> 3; r < rows; r += 4)
                         cp_async16(st + r * kRingPitch, p.vecs + static_cast<size_t>(cids[g0 + r]) * p.row_stride + d);
             }
             asm volatile("cp.async.commit_group;\n" ::: "memory");
         };
-        for (uint32_t c = 0; c + 1 < kRingStages; ++c) issue(c);
+        for (uint32_t c = 0; c + 1 < S; ++c) issue(c);
         float acc = 0.0f;
         for (uint32_t c = 0; c < nch; ++c) {
-            issue(c + kRingStages - 1);
-            asm volatile("cp.async.wait_group %0;\n" ::"n"(kRingStages - 1) : "memory");
+            issue(c + S - 1);
+            asm volatile("cp.async.wait_group %0;\n" ::"n"(S - 1) : "memory");
             __syncwarp();
             if (lane < rows) {
-                const float* x = ring + (c % kRingStages) * 32u * kRingPitch + lane * kRingPitch;
+                const float* x = ring + (c % S) * kRingStageFloats + lane * kRingPitch;
                 const uint32_t d0 = c * kRingCh;
                 const uint32_t n4 = min(kRingCh, p.row_stride - d0) / 4u;
                 for (uint32_t j = 0; j < n4; ++j) {
@@ -113,6 +114,17 @@ __device__ __forceinline__ void score_rows_seq_ring(const SearchParams& p, uint3
         if (lane < rows) cdist[g0 + lane] = acc;
         asm volatile("cp.async.wait_group 0;\n" ::: "memory");
         __syncwarp();
+    }
+}
+
+__device__ __forceinline__ void score_rows_seq_ring(const SearchParams& p, uint32_t m, const uint32_t* cids,
+                                                    float* cdist, const float* qsm, float* ring,
+                                                    unsigned lane) {
+    switch (p.stage_ring) {
+        case 5: score_rows_seq_ring_s<5>(p, m, cids, cdist, qsm, ring, lane); break;
+        case 6: score_rows_seq_ring_s<6>(p, m, cids, cdist, qsm, ring, lane); break;
+        case 8: score_rows_seq_ring_s<8>(p, m, cids, cdist, qsm, ring, lane); break;
+        default: score_rows_seq_ring_s<kRingStages>(p, m, cids, cdist, qsm, ring, lane); break;
     }
 }
 

@@ -364,12 +364,28 @@ cudaError_t plan_search(SearchParams& p, LaunchShape& shape, size_t max_smem_opt
             // wide rows (C4: 3.84 KB): whole-row staging held 12 rows per warp
             // (one 4-warp block per SM, 12 of 32 lanes folding); a ring of row
             // chunks keeps all 32 lanes folding in 18 KB per warp
-            p.stage_ring = 1;
-            p.stage_rows = 0;
-            off = align16(off + dev::kRingFloats * 4u);
             // tens of KB per warp: one warp per block, so that the SM's shared
-            // memory holds as many warps (queries) as fit, not whole blocks
+            // memory holds as many warps (queries) as fit, not whole blocks.
+            // Ring depth: the deepest of 4/5/6/8 chunks at which the launch's
+            // queries still all fit on the SMs at once (a second wave would
+            // cost more than the extra bytes in flight gain); 4 when they do
+            // not fit anyway.
             shape.warps_per_block = 1;
+            p.stage_ring = dev::kRingStages;
+            p.stage_rows = 0;
+            if (p.sm_count > 0 && p.nq > 0) {
+                constexpr uint64_t kSmemPerSm = 233472;   // B200: 228 KB per SM, 1 KB reserved per block
+                const uint64_t per_sm = (static_cast<uint64_t>(p.nq) + p.sm_count - 1) / p.sm_count;
+                const uint32_t depths[3] = {8u, 6u, 5u};
+                for (uint32_t s : depths) {
+                    const uint64_t need = align16(off + s * dev::kRingStageFloats * 4u) + 1024u;
+                    if (need <= max_smem_optin + 1024u && per_sm <= 32u && per_sm * need <= kSmemPerSm) {
+                        p.stage_ring = s;
+                        break;
+                    }
+                }
+            }
+            off = align16(off + p.stage_ring * dev::kRingStageFloats * 4u);
         } else {
             off = align16(off + rows * row_bytes);
         }

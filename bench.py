@@ -272,6 +272,42 @@ def recall_at_k(pred, gt, k=K):
     return hits / (gt.shape[0] * k)
 
 
+CLI_SEARCH = {"filter_capacity": 1024, "max_iterations": 1024, "reset_interval": 16}
+
+
+def run_cli(cli, data, mode, topk, k=None):
+    """One run of a gpu_cli-style binary (ours: bin/gpu_cli; the reference's:
+    oracle/_ref/gpu_cli) with the reference JSON on stdin.  Both load the
+    files, upload the index, run 5 back-to-back searches of all queries with
+    the queries already on the device and print "time: X ms  qps: Y" (wall
+    clock, mean of the 5 launches; reference src/gpu_cli.cu:153-165) and
+    "recall@K: R" against the ground-truth file."""
+    import re
+    cfg = {"data": data, "search": {"mode": mode, "K": k or K, "topk_size": topk, **CLI_SEARCH}}
+    t = time.time()
+    p = subprocess.run([cli], input=json.dumps(cfg), capture_output=True, text=True, timeout=600)
+    m = re.search(r"time: ([0-9.eE+-]+) ms\s+qps: ([0-9.eE+-]+)", p.stdout)
+    r = re.search(r"recall@\d+: ([0-9.eE+-]+)", p.stdout)
+    out = {"mode": mode, "topk_size": topk, "rc": p.returncode,
+           "ms": float(m.group(1)) if m else None, "qps": round(float(m.group(2)), 1) if m else None,
+           "recall@10": float(r.group(1)) if r else None, "wall_s": round(time.time() - t, 2)}
+    if p.returncode and p.stderr.strip():
+        out["stderr"] = p.stderr.strip().splitlines()[-1]
+    return out
+
+
+def write_cli_files(tmp, base, queries, gt, graph):
+    """graph.bin path plus base/query fvecs and a 10-column ground-truth ivecs
+    in `tmp`: the file set both CLIs read."""
+    from beam_search_collab_b200 import datasets as ds
+    data = {"graph": graph, "base": os.path.join(tmp, "base.fvecs"), "query": os.path.join(tmp, "query.fvecs"),
+            "gt": os.path.join(tmp, "gt.ivecs")}
+    ds.write_fvecs(data["base"], base)
+    ds.write_fvecs(data["query"], queries)
+    ds.write_ivecs(data["gt"], np.ascontiguousarray(gt[:, :K]).astype(np.int32))
+    return data
+
+
 # --------------------------------------------------------------- our arm
 
 def query_share(rank, world, strong):
@@ -538,6 +574,17 @@ def run_ours(args, rank, world, local_rank):
         if ref_ids is not None:
             line["parity"] = parity_vs_reference(ref_ids, ids_d.cpu().numpy().view(np.uint32),
                                                  dists_d.cpu().numpy(), base, queries, gt)
+    if not args.no_cli and world == 1 and not codebook and CFG_NAME == "c2":
+        # the drop-in CLI on the same files with the reference CLI's own
+        # timing (the reference arm runs the reference gpu_cli the same way)
+        import beam_search_collab_b200 as Bm
+        with tempfile.TemporaryDirectory() as tmp:
+            data = write_cli_files(tmp, base, queries, gt, os.path.join(DATA_DIR, cfg.get("data_dir", CFG_NAME),
+                                                                         "graph.bin"))
+            runs = [run_cli(Bm.CLI_PATH, data, args.mode, chosen), run_cli(Bm.CLI_PATH, data, args.mode, 64)]
+        line["cli"] = {"binary": "bin/gpu_cli (this build's drop-in CLI)", "runs": runs,
+                       "timing": "the CLI's own: wall clock, mean of 5 searches of all queries, queries on the "
+                                 "device (reference src/gpu_cli.cu:153-165)"}
     return line
 
 
@@ -639,7 +686,8 @@ def run_reference(args, rank, world):
     nq = sum(i["nq"] for i in infos)
     value = nq / secs
     cores = infos[0]["threads"]
-    return {
+    ref_gpu = None if (args.no_cli or world > 1) else reference_gpu(base, queries_all, cfg)
+    line = {
         "impl": "reference",
         "metric": "QPS at recall@10>=0.95",
         "value": round(value, 1),
@@ -659,6 +707,49 @@ def run_reference(args, rank, world):
                          "sample": f"first {sample} queries per step"},
         "e2e": {"value": round(value, 1), "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    if ref_gpu is not None:
+        line["reference_gpu"] = ref_gpu
+    return line
+
+
+# modes and beams of the reference gpu_cli timed beside its CPU search: topk 64
+# is its smallest power-of-two beam at recall@10 >= 0.95 on C2 (its
+# non-power-of-two beams return recall 0), warp2 its fastest mode there
+REF_GPU_RUNS = (("warp2", 64), ("warp4", 64), ("warp1", 64), ("base", 64))
+
+
+def reference_gpu(base, queries, cfg):
+    """The reference's own GPU search (its gpu_cli compiled for sm_100a into
+    oracle/_ref/gpu_cli from the reference sources) on the workload's files,
+    with its own timing; None when it does not apply.  Only K <= degree is
+    run: above it the reference's final flush writes K distances into a
+    degree-sized shared-memory buffer (include/gpu_search_warp.cuh:237,
+    include/gpu_search_base.cuh:246), the illegal address it raised at K=100
+    on the 960-d workload."""
+    cli = os.path.join(ROOT, "oracle", "_ref", "gpu_cli")
+    if CFG_NAME != "c2" or cfg["codebook"]:
+        return None
+    if not os.access(cli, os.X_OK):
+        return {"unavailable": "oracle/_ref/gpu_cli was not built (make -C oracle gpu REF=<reference tree>)"}
+    import torch
+    if not torch.cuda.is_available():
+        return {"unavailable": "no CUDA device"}
+    graph = os.path.join(DATA_DIR, cfg.get("data_dir", CFG_NAME), "graph.bin")
+    # exact top-10 for the CLI's recall line: float64 on the GPU (harness code,
+    # exact for these integer-valued rows)
+    bt = torch.from_numpy(base).cuda()
+    gt = gpu_ground_truth(bt, torch.from_numpy(queries[:NQ_PER_GPU]).cuda(), K)
+    del bt
+    torch.cuda.empty_cache()
+    with tempfile.TemporaryDirectory() as tmp:
+        data = write_cli_files(tmp, base, queries[:NQ_PER_GPU], gt, graph)
+        runs = [run_cli(cli, data, m, t) for m, t in REF_GPU_RUNS]
+    ok = [r for r in runs if r["rc"] == 0 and r["qps"] and (r["recall@10"] or 0) >= TARGET_RECALL]
+    best = max(ok, key=lambda r: r["qps"]) if ok else None
+    return {"binary": "oracle/_ref/gpu_cli (the reference src/gpu_cli.cu, nvcc -arch sm_100a)", "runs": runs,
+            "best_at_recall_0.95": best, "queries": NQ_PER_GPU,
+            "timing": "the CLI's own: wall clock, mean of 5 searches of all queries, queries on the device "
+                      "(reference src/gpu_cli.cu:153-165)"}
 
 
 def profile_run(args):
@@ -1006,6 +1097,8 @@ def main():
     ap.add_argument("--cpu-sample", type=int, default=2000)
     ap.add_argument("--ref-sample", type=int, default=1000)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-cli", action="store_true",
+                    help="skip the gpu_cli runs (ours in our arm, the reference's in the reference arm)")
     ap.add_argument("--sharded", action="store_true",
                     help="C5 shape: an index sharded over the GPUs (see run_sharded)")
     ap.add_argument("--shard-rows", type=int, default=12_500_000)

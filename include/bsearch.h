@@ -89,7 +89,10 @@ typedef struct bs_stats {
     uint32_t block_bytes;     /* bytes per node block copied per expansion
                                  (neighbourhood block, or the RaBitQ node
                                  block; 0: the gather layout was used)       */
-    uint32_t reserved;
+    uint32_t warps_per_query; /* warps that worked on each query: 1 for the
+                                 warp-per-query kernels, 2 or 4 for mode base
+                                 over neighbourhood blocks (one thread block
+                                 per query)                                  */
 } bs_stats;
 
 /* Fills the reference defaults: mode "base", K 100, topk_size 256,
