@@ -69,6 +69,37 @@ constexpr uint32_t kRingPitch = 36;    // floats per staged row chunk: 9 16-byte
 constexpr uint32_t kRingStageFloats = 32u * kRingPitch;
 constexpr uint32_t kRingFloats = kRingStages * kRingStageFloats;
 
+// Sequential fold of one staged row chunk (n4 groups of 4 dimensions from d0)
+// into acc; full chunks are unrolled so that the shared-memory loads run
+// ahead of the dependent additions.
+__device__ __forceinline__ float fold_chunk(float acc, const float* x, const float* qsm, uint32_t d0, uint32_t n4) {
+    if (n4 == kRingCh / 4u) {
+        float4 v[kRingCh / 4u];
+#pragma unroll
+        for (uint32_t j = 0; j < kRingCh / 4u; ++j) v[j] = *reinterpret_cast<const float4*>(x + 4u * j);
+#pragma unroll
+        for (uint32_t j = 0; j < kRingCh / 4u; ++j) {
+            const float4 q = *reinterpret_cast<const float4*>(qsm + d0 + 4u * j);
+            float t;
+            t = __fsub_rn(q.x, v[j].x); acc = __fadd_rn(acc, __fmul_rn(t, t));
+            t = __fsub_rn(q.y, v[j].y); acc = __fadd_rn(acc, __fmul_rn(t, t));
+            t = __fsub_rn(q.z, v[j].z); acc = __fadd_rn(acc, __fmul_rn(t, t));
+            t = __fsub_rn(q.w, v[j].w); acc = __fadd_rn(acc, __fmul_rn(t, t));
+        }
+        return acc;
+    }
+    for (uint32_t j = 0; j < n4; ++j) {
+        const float4 v = *reinterpret_cast<const float4*>(x + 4u * j);
+        const float4 q = *reinterpret_cast<const float4*>(qsm + d0 + 4u * j);
+        float t;
+        t = __fsub_rn(q.x, v.x); acc = __fadd_rn(acc, __fmul_rn(t, t));
+        t = __fsub_rn(q.y, v.y); acc = __fadd_rn(acc, __fmul_rn(t, t));
+        t = __fsub_rn(q.z, v.z); acc = __fadd_rn(acc, __fmul_rn(t, t));
+        t = __fsub_rn(q.w, v.w); acc = __fadd_rn(acc, __fmul_rn(t, t));
+    }
+    return acc;
+}
+
 template <uint32_t S>
 __device__ __forceinline__ void score_rows_seq_ring_s(const SearchParams& p, uint32_t m, const uint32_t* cids,
                                                       float* cdist, const float* qsm, float* ring,
@@ -96,18 +127,9 @@ __device__ __forceinline__ void score_rows_seq_ring_s(const SearchParams& p, uin
             asm volatile("cp.async.wait_group %0;\n" ::"n"(S - 1) : "memory");
             __syncwarp();
             if (lane < rows) {
-                const float* x = ring + (c % S) * kRingStageFloats + lane * kRingPitch;
                 const uint32_t d0 = c * kRingCh;
-                const uint32_t n4 = min(kRingCh, p.row_stride - d0) / 4u;
-                for (uint32_t j = 0; j < n4; ++j) {
-                    const float4 v = *reinterpret_cast<const float4*>(x + 4u * j);
-                    const float4 q = *reinterpret_cast<const float4*>(qsm + d0 + 4u * j);
-                    float t;
-                    t = __fsub_rn(q.x, v.x); acc = __fadd_rn(acc, __fmul_rn(t, t));
-                    t = __fsub_rn(q.y, v.y); acc = __fadd_rn(acc, __fmul_rn(t, t));
-                    t = __fsub_rn(q.z, v.z); acc = __fadd_rn(acc, __fmul_rn(t, t));
-                    t = __fsub_rn(q.w, v.w); acc = __fadd_rn(acc, __fmul_rn(t, t));
-                }
+                acc = fold_chunk(acc, ring + (c % S) * kRingStageFloats + lane * kRingPitch, qsm, d0,
+                                 min(kRingCh, p.row_stride - d0) / 4u);
             }
             __syncwarp();   // this stage is refilled by the next iteration's issue
         }

@@ -49,7 +49,6 @@ __global__ void __launch_bounds__(256) k_search_l2(const SearchParams p) {
     const uint32_t fshift = 32u - static_cast<uint32_t>(__popc(fmask));
     const unsigned lt_mask = (1u << lane) - 1u;
     unsigned err = 0;
-
     for (;;) {
         unsigned qi = 0;
         if (lane == 0) qi = atomicAdd(&p.counters->next_query, 1u);
@@ -81,14 +80,18 @@ __global__ void __launch_bounds__(256) k_search_l2(const SearchParams p) {
         __syncwarp();
 
         for (int iter = 0; iter < p.max_iterations; ++iter) {
-            uint32_t cur;
-            if (!beam_pick<RX>(beam, lane, cur)) break;
+            uint32_t cur, nxt;
+            if (!beam_pick_next<RX>(beam, lane, cur, nxt)) break;
             ++E;
             __syncwarp();   // previous round's cids/cdist reads are done
 
             uint32_t c[RY];
             bool fresh[RY];
             const uint32_t* row = p.adj + static_cast<size_t>(cur) * deg;
+            // the adjacency row the next expansion reads unless a better
+            // candidate turns up: start it towards L2 now
+            if (lane == 0 && nxt != kNoNode)
+                asm volatile("prefetch.global.L2 [%0];\n" ::"l"(p.adj + static_cast<size_t>(nxt) * deg));
 #pragma unroll
             for (int r = 0; r < RY; ++r) {
                 const uint32_t pos = static_cast<uint32_t>(r) * 32u + lane;
@@ -168,7 +171,11 @@ __global__ void __launch_bounds__(256) k_search_l2(const SearchParams p) {
                 }
                 if (cnt) {
                     __syncwarp();
-                    beam_merge_compact<RX, RY>(beam, ckeys, cnt, lane, p.topk);
+                    // wide beams: lane stages as loops and only the beam's
+                    // affected suffix merged (same result, a fraction of the
+                    // code and of the stages)
+                    if (RX >= 8) beam_merge_compact_wide<RX, RY>(beam, ckeys, cnt, lane, p.topk);
+                    else beam_merge_compact<RX, RY>(beam, ckeys, cnt, lane, p.topk);
                 }
             }
 

@@ -297,7 +297,8 @@ __global__ void __launch_bounds__(32 * NW, (RX >= 8 ? 16 : 32) / NW) k_search_bq
             if (cnt) {
                 filled += cnt;
                 __syncwarp();
-                beam_merge_compact<RX, RY>(beam, ckeys, cnt, lane, p.topk);
+                if (RX >= 8) beam_merge_compact_wide<RX, RY>(beam, ckeys, cnt, lane, p.topk);
+                else beam_merge_compact<RX, RY>(beam, ckeys, cnt, lane, p.topk);
             }
         }
 

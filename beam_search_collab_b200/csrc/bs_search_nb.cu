@@ -209,7 +209,8 @@ __global__ void __launch_bounds__(256) k_search_nb(const SearchParams p) {
             if (cnt) {
                 filled += cnt;
                 __syncwarp();
-                beam_merge_compact<RX, RY>(beam, ckeys, cnt, lane, p.topk);
+                if (RX >= 8) beam_merge_compact_wide<RX, RY>(beam, ckeys, cnt, lane, p.topk);
+                else beam_merge_compact<RX, RY>(beam, ckeys, cnt, lane, p.topk);
             }
 
             if (FM == kBloom && p.reset_interval > 0 && (iter + 1) % p.reset_interval == 0) {
