@@ -1088,7 +1088,7 @@ BS_API bs_status bs_index_build_graph(bs_index* ix, const bs_graph_build_params*
         return fail(BS_ERR_UNSUPPORTED, "rows of %d dimensions do not fit the graph builder's shared memory", ix->dim);
     const uint64_t bound = std::max<uint64_t>(1, static_cast<uint64_t>(0.02 * static_cast<double>(n)));
     const uint64_t batch_max = std::max<uint64_t>(1, std::min<uint64_t>(bound, n > 1 ? n - 1 : 1));
-    constexpr uint32_t kPoolCap = 2048, kLogCap = 8192;
+    constexpr uint32_t kPoolCap = 2048, kLogCap = 8192, kOvfCap = 65536;
     uint32_t cap_warps = bsb::graph_build_search_warps(a, ix->num_sms, ix->smem_optin);
     if (cap_warps == 0) return fail(BS_ERR_UNSUPPORTED, "graph builder launch shape");
     const uint32_t words = static_cast<uint32_t>(((n + 31u) / 32u + 3u) & ~3ull);
@@ -1111,13 +1111,13 @@ BS_API bs_status bs_index_build_graph(bs_index* ix, const bs_graph_build_params*
         (e = cudaMalloc(&d_cnt, n * 4)) != cudaSuccess || (e = cudaMalloc(&d_pool, batch_max * kPoolCap * 8)) != cudaSuccess ||
         (e = cudaMalloc(&d_pcnt, batch_max * 4)) != cudaSuccess || (e = cudaMalloc(&d_vis, vis_warps * per_warp)) != cudaSuccess ||
         (e = cudaMalloc(&d_rev, items * 4 * 5)) != cudaSuccess || (e = cudaMalloc(&d_sort, sort_bytes + 16)) != cudaSuccess ||
-        (e = cudaMalloc(&d_misc, 256)) != cudaSuccess) {
+        (e = cudaMalloc(&d_misc, 256 + 4 * kOvfCap)) != cudaSuccess) {
         cleanup();
         return cuda_fail(e, "graph builder buffers");
     }
     if ((e = cudaMemcpy(d_order, order.data(), n * 4, cudaMemcpyHostToDevice)) != cudaSuccess ||
         (e = cudaMemset(d_cnt, 0, n * 4)) != cudaSuccess || (e = cudaMemset(d_vis, 0, vis_warps * per_warp)) != cudaSuccess ||
-        (e = cudaMemset(d_misc, 0, 256)) != cudaSuccess) {
+        (e = cudaMemset(d_misc, 0, 256 + 4 * kOvfCap)) != cudaSuccess) {
         cleanup();
         return cuda_fail(e, "graph builder set-up");
     }
@@ -1136,6 +1136,16 @@ BS_API bs_status bs_index_build_graph(bs_index* ix, const bs_graph_build_params*
     a.seg_start = rev + 4 * items;
     a.seg_count = static_cast<uint32_t*>(d_misc);
     a.err = static_cast<unsigned int*>(d_misc) + 4;
+    a.ovf_count = static_cast<uint32_t*>(d_misc) + 8;
+    a.ovf_jobs = static_cast<uint32_t*>(d_misc) + 64;
+    a.ovf_cap = kOvfCap;
+    a.ovf_pass = 0;
+    // BSEARCH_GB_REV_PRUNE_CAP (a power of two, 64..4096): a smaller first
+    // reverse-prune launch, so that tests reach the second launch on small graphs
+    if (const char* c = std::getenv("BSEARCH_GB_REV_PRUNE_CAP")) {
+        const uint32_t v = static_cast<uint32_t>(std::strtoul(c, nullptr, 10));
+        if (v >= 64 && v <= 4096 && (v & (v - 1)) == 0) a.rev_prune_cap = v;
+    }
     // the batch loop (src/build_graph.cpp:303-369)
     for (uint64_t start = 1; start < n;) {
         const uint64_t end = std::min(std::min(start * 2, start + bound), n);
@@ -1154,7 +1164,7 @@ BS_API bs_status bs_index_build_graph(bs_index* ix, const bs_graph_build_params*
         cleanup();
         return fail(BS_ERR_KERNEL, "graph builder: %s (flags 0x%x)",
                     (err & bsb::kErrPoolFull) ? "a build search expanded more than 2048 nodes"
-                                              : "a prune had more than 4096 candidates", err);
+                                              : "a prune had more than 16384 candidates", err);
     }
     // missing slots are node 0 (src/build_graph.cpp:371): the tails past each count
     {

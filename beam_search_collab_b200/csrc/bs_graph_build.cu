@@ -378,9 +378,10 @@ __global__ void __launch_bounds__(32) k_gb_prune(const GraphBuildArgs a, unsigne
     s.kept_flag = p;
     unsigned err = 0;
     uint32_t segs = 0;
-    if (JOB == kJobReverse) segs = *a.seg_count;
+    if (JOB == kJobReverse) segs = a.ovf_pass ? *a.ovf_count : *a.seg_count;
     const unsigned long long jobs = JOB == kJobReverse ? segs : njobs;
-    for (unsigned long long job = blockIdx.x; job < jobs; job += gridDim.x) {
+    for (unsigned long long it = blockIdx.x; it < jobs; it += gridDim.x) {
+        const unsigned long long job = (JOB == kJobReverse && a.ovf_pass) ? a.ovf_jobs[it] : it;
         uint32_t u, c = 0;
         if (JOB == kJobTargets) {
             u = a.order[a.start + job];
@@ -423,7 +424,23 @@ __global__ void __launch_bounds__(32) k_gb_prune(const GraphBuildArgs a, unsigne
                 continue;
             }
             c = have + k;
-            if (c > a.prune_cap) { err |= kErrPruneFull; continue; }
+            if (c > a.prune_cap) {
+                // too many for this launch's shared memory: to the second
+                // launch's list (prunes of different nodes are independent)
+                if (!a.ovf_pass && a.ovf_jobs) {
+                    uint32_t at = 0;
+                    if (lane == 0) at = atomicAdd(a.ovf_count, 1u);
+                    at = __shfl_sync(kFull, at, 0);
+                    if (at < a.ovf_cap) {
+                        if (lane == 0) a.ovf_jobs[at] = static_cast<uint32_t>(job);
+                    } else {
+                        err |= kErrPruneFull;
+                    }
+                } else {
+                    err |= kErrPruneFull;
+                }
+                continue;
+            }
             for (uint32_t i = lane; i < have; i += 32) s.keys[i] = pkey(dists[i], ids[i]);
             for (uint32_t j = lane; j < k; j += 32) {
                 const uint32_t t = a.rev_t[b + j];
@@ -579,7 +596,6 @@ uint32_t graph_build_search_warps(const GraphBuildArgs& a, int num_sms, size_t s
 cudaError_t graph_build_batch(GraphBuildArgs& a, size_t smem_optin, int num_sms, void* sort_tmp, size_t sort_tmp_bytes,
                               uint32_t* rev_keys_in, uint32_t* rev_vals_in, uint32_t* rev_keys_out,
                               uint32_t* rev_vals_out, cudaStream_t stream) {
-    (void)smem_optin;
     SearchFn fn = select_gb(a.L, dm_of(a));
     if (!fn) return cudaErrorInvalidValue;
     // 1. searches: one warp per target
@@ -605,8 +621,20 @@ cudaError_t graph_build_batch(GraphBuildArgs& a, size_t smem_optin, int num_sms,
     if ((e = cudaMemsetAsync(a.seg_count, 0, 4, stream)) != cudaSuccess) return e;
     k_gb_segments<<<tb, 256, 0, stream>>>(a);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    // 4. append, or prune the lists that grow past the degree
-    return launch_prune<kJobReverse>(a, 0, num_sms, stream);
+    // 4. append, or prune the lists that grow past the degree; then the
+    // prunes too large for the first launch, with the large candidate array
+    if (a.ovf_jobs && (e = cudaMemsetAsync(a.ovf_count, 0, 4, stream)) != cudaSuccess) return e;
+    {
+        GraphBuildArgs first = a;
+        if (a.rev_prune_cap && a.rev_prune_cap < a.prune_cap) first.prune_cap = a.rev_prune_cap;
+        if ((e = launch_prune<kJobReverse>(first, 0, num_sms, stream)) != cudaSuccess) return e;
+    }
+    if (!a.ovf_jobs) return cudaSuccess;
+    GraphBuildArgs big = a;
+    big.prune_cap = kGraphBigPruneCap;
+    big.ovf_pass = 1;
+    if (prune_smem(big) > smem_optin) return cudaSuccess;   // the first launch flagged them already
+    return launch_prune<kJobReverse>(big, 0, num_sms, stream);
 }
 
 cudaError_t graph_build_finish(GraphBuildArgs& a, size_t smem_optin, int num_sms, cudaStream_t stream) {

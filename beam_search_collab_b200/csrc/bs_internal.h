@@ -259,7 +259,16 @@ struct GraphBuildArgs {
     uint32_t* seg_count;         // [1] number of segments
     uint32_t prune_cap;          // candidates a prune holds (shared memory)
     unsigned int* err;           // error bits (kErrPoolFull, kErrPruneFull)
+    // reverse-edge prunes with more candidates than prune_cap (a node that
+    // receives thousands of reverse edges in one batch) are listed here and
+    // run by a second launch with kGraphBigPruneCap candidates
+    uint32_t* ovf_jobs;          // [ovf_cap] segment indices
+    uint32_t* ovf_count;         // [1]
+    uint32_t ovf_cap;
+    uint32_t ovf_pass;           // 1: this launch runs the listed segments
+    uint32_t rev_prune_cap;      // first reverse launch's candidate array (0: prune_cap; tests set it small)
 };
+constexpr uint32_t kGraphBigPruneCap = 16384;
 constexpr unsigned kErrPoolFull = 16u;    // a build search expanded more than pool_cap nodes
 constexpr unsigned kErrPruneFull = 32u;   // a prune had more than prune_cap candidates
 

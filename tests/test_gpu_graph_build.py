@@ -87,3 +87,28 @@ def test_build_graph_cli_writes_the_reference_file(tmp_path):
     r = subprocess.run([cli, "--base", g.files["base"], "--graph", out, "--metric", "cosine"],
                        capture_output=True, text=True)
     assert r.returncode == 1 and "Unsupported metric: cosine" in r.stderr
+
+
+def test_large_reverse_prunes_take_the_second_launch(tmp_path, monkeypatch):
+    """A node that receives more reverse edges in one batch than the first
+    reverse-prune launch holds (4,096 candidates; here 64 through
+    BSEARCH_GB_REV_PRUNE_CAP) is pruned by a second launch with a larger
+    candidate array: the graph stays identical, edge for edge, to the default
+    build and to the reference tool's."""
+    rng = np.random.default_rng(2024)
+    centres = rng.normal(size=(20, 32)).astype(np.float32) * 4
+    base = (centres[rng.integers(0, 20, 20000)] + rng.normal(size=(20000, 32))).astype(np.float32)
+    ix = B.Index.from_vectors(base, 32)
+    try:
+        default = ix.build_graph(beam_width=64, alpha=1.2, seed=5)
+    finally:
+        ix.close()
+    monkeypatch.setenv("BSEARCH_GB_REV_PRUNE_CAP", "64")
+    ix = B.Index.from_vectors(base, 32)
+    try:
+        small = ix.build_graph(beam_width=64, alpha=1.2, seed=5)
+    finally:
+        ix.close()
+    assert np.array_equal(small, default)
+    ref = _reference_graph(base, tmp_path, 32, 64, 1.2, 5)
+    assert np.array_equal(default, ref)
