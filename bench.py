@@ -1011,6 +1011,122 @@ def run_sharded(args, rank, world, local_rank):
     }
 
 
+def run_replicated(args, rank, world, local_rank):
+    """--replicated: the C5 companion run.  A 10M-row index of the C5
+    distribution (one draw, the same on every rank) is built on every GPU
+    (GPU graph builder and codebook builder, the reference algorithms and
+    seeds: the same graph on every rank, checked by a checksum), and the
+    100,000 queries are split over the ranks (contiguous ranges; rabitq, K 10,
+    topk 256).  value = all queries / max-over-ranks step time (strong
+    scaling: the job is fixed); e2e = the same with page-locked host query and
+    result buffers.  recall@10 on a sample of rank 0's queries against the
+    exact top-10 (bs_ground_truth)."""
+    import torch
+    import torch.distributed as dist
+    import beam_search_collab_b200 as B
+    from beam_search_collab_b200 import datasets as ds
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    rows, nq, K_, topk = args.replicated_rows, args.sharded_nq, 10, args.topk or 256
+    t0 = time.time()
+    s = ds.gen_c5_shard(0, rows, nq)
+    t_data = time.time() - t0
+    ix = B.Index.from_vectors(s.base, 32, device=local_rank)
+    t0 = time.time()
+    edges = ix.build_graph(beam_width=128, alpha=2.0, seed=1234)
+    t_graph = time.time() - t0
+    ix.build_codebook(12345)
+    torch.cuda.synchronize()
+    csum = int(np.bitwise_xor.reduce((edges.astype(np.uint64) * np.uint64(2654435761)).ravel() ^
+                                     np.arange(edges.size, dtype=np.uint64)) & np.uint64((1 << 62) - 1))
+    same_graph = True
+    if world > 1:
+        t = torch.tensor([csum], dtype=torch.int64, device=dev)
+        ts = [torch.empty_like(t) for _ in range(world)]
+        dist.all_gather(ts, t)
+        same_graph = all(int(x) == csum for x in ts)
+    log(f"[rank {rank}] replicated index of {rows} rows: data {t_data:.1f}s, graph {t_graph:.1f}s")
+    q0, q1 = rank * nq // world, (rank + 1) * nq // world
+    mine = np.ascontiguousarray(s.queries[q0:q1])
+    n_mine = len(mine)
+    q = torch.from_numpy(mine).to(dev)
+    params = B.SearchParams(mode="rabitq", K=K_, topk_size=topk)
+    ids = torch.empty((n_mine, K_), dtype=torch.int32, device=dev)
+    dists = torch.empty((n_mine, K_), dtype=torch.float32, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+
+    def step(qp, ip, dp):
+        ix.search_raw(qp, n_mine, ip, dp, params, stream=stream.cuda_stream)
+
+    for _ in range(args.warmup):
+        step(q.data_ptr(), ids.data_ptr(), dists.data_ptr())
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    with ClockSampler(local_rank) as clk:
+        with torch.cuda.stream(stream):
+            for i in range(args.steps):
+                flush.zero_()
+                ev[i][0].record(stream)
+                step(q.data_ptr(), ids.data_ptr(), dists.data_ptr())
+                ev[i][1].record(stream)
+        torch.cuda.synchronize()
+    ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
+    errs = ix.take_errors(stream.cuda_stream)
+    # e2e: page-locked host buffers through the same call
+    hq = torch.from_numpy(mine).pin_memory()
+    hid = torch.empty((n_mine, K_), dtype=torch.int32).pin_memory()
+    hd = torch.empty((n_mine, K_), dtype=torch.float32).pin_memory()
+    step(hq.data_ptr(), hid.data_ptr(), hd.data_ptr())
+    torch.cuda.synchronize()
+    ee = []
+    for _ in range(max(3, min(args.steps, 5))):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        step(hq.data_ptr(), hid.data_ptr(), hd.data_ptr())
+        b.record(stream)
+        b.synchronize()
+        ee.append(a.elapsed_time(b))
+    e2e_ms = statistics.mean(ee)
+    errs |= ix.take_errors(stream.cuda_stream)
+    assert np.array_equal(hid.numpy(), ids.cpu().numpy()), "host-buffer results differ"
+    t = torch.tensor([ms, e2e_ms, float(errs)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.barrier()
+    ms, e2e_ms, errs = float(t[0]), float(t[1]), int(t[2])
+    if errs:
+        raise SystemExit(f"search kernels reported error flags {errs:#x}")
+    if rank != 0:
+        return None
+    ns = min(args.cpu_sample, n_mine)
+    gt_i, _ = ix.ground_truth(q[:ns], 10, with_dists=False)
+    torch.cuda.synchronize()
+    recall = recall_at_k(ids[:ns].cpu().numpy().view(np.uint32).astype(np.int64),
+                         gt_i.cpu().numpy().view(np.uint32).astype(np.int64))
+    return {
+        "metric": "QPS (C5-10M replicated index, queries split over the GPUs)",
+        "value": round(nq / (ms / 1e3), 1), "unit": "queries/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "u8",
+        "data": "synthetic: seeded C5 mixture (4,096 Gaussians, ints 0..255), one draw of "
+                f"{rows} rows; graph and codebook built on every GPU with the reference algorithms",
+        "config": {"workload": f"C5-10M: {rows} x 128 replicated on {world} GPU(s), {nq} queries split over them, "
+                               f"rabitq K {K_} topk {topk}",
+                   "queries_per_gpu": n_mine, "recall@10": round(recall, 5), "recall_sample": ns,
+                   "graph_build_s": round(t_graph, 2), "graph_identical_on_all_ranks": same_graph,
+                   "l2": "256 MiB write before every timed step (outside the timed window)",
+                   "parallelism": f"query-sharded dp{world}, replicated index"},
+        "e2e": {"value": round(nq / (e2e_ms / 1e3), 1), "unit": "queries/s",
+                "h2d_bytes_per_step": int(nq * 128 * 4), "d2h_bytes_per_step": int(nq * K_ * 8)},
+        "gpu_launches": args.steps,
+        "clocks": clk.summary(),
+    }
+
+
 def measure_graph(args):
     """--measure graph: the GPU graph builder (bs_index_build_graph) over the
     workload's base, against the graph the reference build_graph wrote for it
@@ -1102,6 +1218,9 @@ def main():
     ap.add_argument("--sharded", action="store_true",
                     help="C5 shape: an index sharded over the GPUs (see run_sharded)")
     ap.add_argument("--shard-rows", type=int, default=12_500_000)
+    ap.add_argument("--replicated", action="store_true",
+                    help="C5-10M: one index replicated on every GPU, the queries split over them")
+    ap.add_argument("--replicated-rows", type=int, default=10_000_000)
     ap.add_argument("--sharded-nq", type=int, default=100_000)
     ap.add_argument("--scaling", choices=("weak", "strong"), default="weak",
                     help="weak: every GPU searches its own 10,000 queries; strong: the workload's 10,000 "
@@ -1138,6 +1257,8 @@ def main():
         line = run_reference(args, rank, world)
     elif args.sharded:
         line = run_sharded(args, rank, world, local_rank)
+    elif args.replicated:
+        line = run_replicated(args, rank, world, local_rank)
     else:
         line = run_ours(args, rank, world, local_rank)
     if world > 1 and args.impl == "ours":
