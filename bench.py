@@ -769,6 +769,14 @@ def profile_run(args):
         return
     base, queries, edges, codebook = config_data(CFG_NAME, NQ_PER_GPU)
     ix = B.Index.from_arrays(base, edges)
+    if args.measure == "ground_truth":
+        # the exact brute force (bs_ground_truth): `warmup` runs and one more
+        q = torch.from_numpy(queries).cuda()
+        for _ in range(args.warmup + 1):
+            ix.ground_truth(q, 10, with_dists=False)
+        torch.cuda.synchronize()
+        log("profile run done")
+        return
     if codebook:
         ix.load_codebook(codebook)
     ix.entry_point()
@@ -1225,7 +1233,7 @@ def main():
     ap.add_argument("--scaling", choices=("weak", "strong"), default="weak",
                     help="weak: every GPU searches its own 10,000 queries; strong: the workload's 10,000 "
                          "queries split over the GPUs")
-    ap.add_argument("--measure", choices=("search", "codebook", "graph"), default="search",
+    ap.add_argument("--measure", choices=("search", "codebook", "graph", "ground_truth"), default="search",
                     help="codebook / graph: time the GPU codebook or graph builder instead of the search")
     ap.add_argument("--profile-run", action="store_true",
                     help="for ncu: build the index, run `--warmup` searches and one more, print nothing else")
