@@ -15,6 +15,34 @@ __device__ __forceinline__ const float* query_src(const SearchParams& p, uint32_
     return (p.queries_src != nullptr ? p.queries_src : p.queries) + static_cast<size_t>(qi) * p.dim;
 }
 
+// A query row read from host memory mapped into the device (page-locked
+// buffers used in place) into its device slot: every load of a thread is
+// issued before its stores, so the row crosses the bus in one round trip
+// (16-byte loads when the row allows them) instead of one per 32 elements.
+__device__ __forceinline__ void copy_query_row(float* __restrict__ slot, const float* __restrict__ q, uint32_t dim,
+                                               unsigned t, unsigned nt) {
+    if ((dim & 3u) == 0u && ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(slot)) & 15u) == 0u) {
+        const float4* q4 = reinterpret_cast<const float4*>(q);
+        float4* s4 = reinterpret_cast<float4*>(slot);
+        const uint32_t n4 = dim / 4u;
+        for (uint32_t b = 0; b < n4; b += 4u * nt) {
+            float4 v[4];
+#pragma unroll
+            for (uint32_t j = 0; j < 4u; ++j) {
+                const uint32_t i = b + j * nt + t;
+                if (i < n4) v[j] = q4[i];
+            }
+#pragma unroll
+            for (uint32_t j = 0; j < 4u; ++j) {
+                const uint32_t i = b + j * nt + t;
+                if (i < n4) s4[i] = v[j];
+            }
+        }
+        return;
+    }
+    for (uint32_t d = t; d < dim; d += nt) slot[d] = q[d];
+}
+
 // Whole-warp test of the integer-exact condition for the query in smem:
 // every value an integer in [qlo, qhi].  The host derives that range from the
 // base vectors' own range so that every |q_d - x_d| <= B with

@@ -148,7 +148,7 @@ __global__ void __launch_bounds__(32 * NW, (RX >= 8 ? 16 : 32) / NW) k_search_bq
         if (DM == kU8 && p.queries_src != nullptr) {
             // read over the bus once, into this query's device slot
             float* slot = const_cast<float*>(p.queries) + static_cast<size_t>(qi) * p.dim;
-            for (uint32_t d = tid; d < p.dim; d += 32u * NW) slot[d] = q[d];
+            copy_query_row(slot, q, p.dim, tid, 32u * NW);
             q = slot;
         }
         const float* qv = DM == kU8 ? q : qsm;

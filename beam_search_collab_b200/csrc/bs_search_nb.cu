@@ -87,7 +87,7 @@ __global__ void __launch_bounds__(256) k_search_nb(const SearchParams p) {
         if (DM == kU8 && p.queries_src != nullptr) {
             // read over the bus once, into this query's device slot
             float* slot = const_cast<float*>(p.queries) + static_cast<size_t>(qi) * p.dim;
-            for (uint32_t d = lane; d < p.dim; d += 32) slot[d] = q[d];
+            copy_query_row(slot, q, p.dim, lane, 32u);
             __syncwarp();
             q = slot;
         }

@@ -112,6 +112,26 @@ CONFIGS = {
 CFG_NAME = "c2"
 
 
+def build_missing_graph(base, graph):
+    """A workload's graph.bin when it is not in bench_data/ yet: the reference
+    settings (degree 32, beam 128, alpha 2.0, seed 1234) through the GPU graph
+    builder, whose file equals the reference build_graph's edge for edge
+    (tests/test_gpu_graph_build.py; all 1,000,000 rows of the C2 graph)."""
+    import beam_search_collab_b200 as B
+    log(f"building {graph} on the GPU (reference build_graph settings)")
+    os.makedirs(os.path.dirname(graph), exist_ok=True)
+    ix = B.Index.from_vectors(base, 32)
+    try:
+        edges = ix.build_graph(beam_width=128, alpha=2.0, seed=1234)
+    finally:
+        ix.close()
+    tmp = graph + ".tmp"
+    with open(tmp, "wb") as f:
+        np.array([base.shape[0], 32], dtype=np.int32).tofile(f)
+        np.ascontiguousarray(edges, dtype=np.uint32).tofile(f)
+    os.replace(tmp, graph)
+
+
 def config_data(name: str, nq_total: int):
     """Base, queries, graph edges and codebook path (or None) of a workload;
     graphs and codebooks are built once with the reference tools into
@@ -122,7 +142,7 @@ def config_data(name: str, nq_total: int):
     ddir = os.path.join(DATA_DIR, cfg.get("data_dir", name))
     graph = os.path.join(ddir, "graph.bin")
     if not os.path.exists(graph):
-        raise SystemExit(f"missing {graph}: build it with the reference build_graph over the {name} base")
+        build_missing_graph(s.base, graph)
     cb = os.path.join(ddir, "codebook.bin") if cfg["codebook"] else None
     if cb and not os.path.exists(cb):
         # too large to ship (2.4 GB for C3): the reference build_rabitq makes it here
@@ -465,20 +485,21 @@ def run_ours(args, rank, world, local_rank):
     hq = torch.from_numpy(queries).pin_memory()
     hid = torch.empty((nq, K), dtype=torch.int32).pin_memory()
     hdist = torch.empty((nq, K), dtype=torch.float32).pin_memory()
-    e2e_steps = max(3, min(args.steps, 10))
+    # (steps enqueued back to back as for `value`: each step's kernel reads its
+    # queries from the page-locked buffer over the bus and writes its result
+    # rows back into page-locked memory, inside the step's events)
+    e2e_steps = max(3, min(args.steps, 20))
     for _ in range(2):
         ix.search_raw(hq.data_ptr(), nq, hid.data_ptr(), hdist.data_ptr(), params, stream=stream.cuda_stream)
-    ee = []
-    for _ in range(e2e_steps):
-        with torch.cuda.stream(stream):
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(e2e_steps)]
+    with torch.cuda.stream(stream):
+        for a, b in evs:
             flush.zero_()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(stream)
-        ix.search_raw(hq.data_ptr(), nq, hid.data_ptr(), hdist.data_ptr(), params, stream=stream.cuda_stream)
-        b.record(stream)
-        b.synchronize()
-        ee.append(a.elapsed_time(b))
-    e2e_ms = statistics.mean(ee)
+            a.record(stream)
+            ix.search_raw(hq.data_ptr(), nq, hid.data_ptr(), hdist.data_ptr(), params, stream=stream.cuda_stream)
+            b.record(stream)
+    stream.synchronize()
+    e2e_ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
     assert np.array_equal(hid.numpy(), ids_d.cpu().numpy()), "e2e results differ from device-resident results"
     kernel_errors |= ix.take_errors(stream.cuda_stream)
 
