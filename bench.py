@@ -520,8 +520,9 @@ def run_ours(args, rank, world, local_rank):
     achieved = alg_bytes / (statistics.mean(step_ms) / 1e3) / 1e9
     achieved_useful = useful_bytes / (statistics.mean(step_ms) / 1e3) / 1e9
     traffic = None
-    # DRAM bytes of one launch of this kernel on this workload, from the ncu
-    # capture summarised in profiles/k_search_nb_c2.md
+    # DRAM bytes of one launch of this kernel on this workload
+    # (dram__bytes_read.sum + dram__bytes_write.sum of an ncu capture of the
+    # same launch, kept beside the ncu summaries)
     tp = os.path.join(ROOT, "profiles", f"traffic_{CFG_NAME}.json")
     if os.path.exists(tp) and not strong and world == 1:
         with open(tp) as f:
