@@ -789,6 +789,18 @@ def profile_run(args):
         torch.cuda.synchronize()
         log("profile run done")
         return
+    if args.measure == "graph":
+        # the graph builder's kernels: `warmup` builds and one more (the
+        # builder's reference settings)
+        from beam_search_collab_b200 import datasets as ds
+        s = getattr(ds, CONFIGS[CFG_NAME]["gen"])(nq=1, **CONFIGS[CFG_NAME].get("gen_kwargs", {}))
+        for _ in range(args.warmup + 1):
+            gx = B.Index.from_vectors(s.base, 32)
+            gx.build_graph(beam_width=128, alpha=2.0, seed=1234)
+            gx.close()
+        torch.cuda.synchronize()
+        log("profile run done")
+        return
     base, queries, edges, codebook = config_data(CFG_NAME, NQ_PER_GPU)
     ix = B.Index.from_arrays(base, edges)
     if args.measure == "ground_truth":
