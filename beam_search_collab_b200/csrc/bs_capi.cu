@@ -1140,8 +1140,12 @@ BS_API bs_status bs_index_build_graph(bs_index* ix, const bs_graph_build_params*
     a.ovf_jobs = static_cast<uint32_t*>(d_misc) + 64;
     a.ovf_cap = kOvfCap;
     a.ovf_pass = 0;
-    // BSEARCH_GB_REV_PRUNE_CAP (a power of two, 64..4096): a smaller first
-    // reverse-prune launch, so that tests reach the second launch on small graphs
+    // The first reverse-prune launch holds 512 candidates per prune (a node's
+    // list plus the reverse edges one batch gives it: rarely more), so that
+    // many prunes share an SM; larger ones run in the second launch.
+    // BSEARCH_GB_REV_PRUNE_CAP (a power of two, 64..4096) sets it (tests use
+    // a small one to reach the second launch on small graphs).
+    a.rev_prune_cap = 512;
     if (const char* c = std::getenv("BSEARCH_GB_REV_PRUNE_CAP")) {
         const uint32_t v = static_cast<uint32_t>(std::strtoul(c, nullptr, 10));
         if (v >= 64 && v <= 4096 && (v & (v - 1)) == 0) a.rev_prune_cap = v;

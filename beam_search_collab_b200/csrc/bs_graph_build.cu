@@ -211,7 +211,18 @@ struct PruneSmem {
     uint32_t* crow8;
     uint32_t* kept_ids;
     float* kept_dist;
+    uint32_t* krow8;     // byte rows of the kept candidates (null: read from global memory)
 };
+
+// Byte rows of the kept candidates are cached in shared memory when they take
+// at most this many bytes (degree x row bytes): every domination test then
+// reads them there instead of from L2.
+constexpr uint32_t kKeptRowCacheBytes = 8192;
+
+__host__ __device__ inline uint32_t kept_row_cache_bytes(const GraphBuildArgs& a) {
+    const uint32_t b = a.degree * a.sp.row_bytes;
+    return (a.sp.vecs8 != nullptr && b <= kKeptRowCacheBytes) ? b : 0u;
+}
 
 __device__ __forceinline__ void warp_sort_keys(unsigned long long* k, uint32_t P, unsigned lane) {
     for (uint32_t size = 2; size <= P; size <<= 1) {
@@ -229,12 +240,14 @@ __device__ __forceinline__ void warp_sort_keys(unsigned long long* k, uint32_t P
     }
 }
 
-// d(kept row, candidate row) by one lane, the reference's value.
+// d(kept row, candidate row) by one lane, the reference's value; byte rows
+// come from krow (the kept row cached in shared memory) when it is given.
 template <int DM>
 __device__ __forceinline__ float pair_dist(const SearchParams& sp, uint32_t kept, const float* crow,
-                                           const uint32_t* crow8, bool int_ok) {
+                                           const uint32_t* crow8, bool int_ok, const uint32_t* krow) {
     if (DM == kU8 && int_ok) {
-        const uint32_t* x = reinterpret_cast<const uint32_t*>(sp.vecs8 + static_cast<size_t>(kept) * sp.row_bytes);
+        const uint32_t* x = krow ? krow
+                                 : reinterpret_cast<const uint32_t*>(sp.vecs8 + static_cast<size_t>(kept) * sp.row_bytes);
         unsigned acc = 0u;
         for (uint32_t w = 0; w < sp.row_bytes / 4u; ++w) {
             const unsigned d = __vabsdiffu4(x[w], crow8[w]);
@@ -243,7 +256,7 @@ __device__ __forceinline__ float pair_dist(const SearchParams& sp, uint32_t kept
         return static_cast<float>(acc);
     }
     if (DM == kU8) {
-        const uint8_t* x = sp.vecs8 + static_cast<size_t>(kept) * sp.row_bytes;
+        const uint8_t* x = krow ? reinterpret_cast<const uint8_t*>(krow) : sp.vecs8 + static_cast<size_t>(kept) * sp.row_bytes;
         float s = 0.0f;
         for (uint32_t d = 0; d < sp.dim; ++d) {
             const float t = __fsub_rn(static_cast<float>(x[d]), crow[d]);
@@ -333,8 +346,10 @@ __device__ void prune_and_store(const GraphBuildArgs& a, uint32_t u, uint32_t c,
             __syncwarp();
             int_ok = DM != kSeq && query_integer_exact(s.crow, sp.dim, sp.team_qlo, sp.team_qhi);
             bool dom = false;
+            const uint32_t words = sp.row_bytes / 4u;
             for (uint32_t k = lane; k < kn; k += 32) {
-                const float dk = pair_dist<DM>(sp, s.kept_ids[k], s.crow, s.crow8, int_ok);
+                const float dk = pair_dist<DM>(sp, s.kept_ids[k], s.crow, s.crow8, int_ok,
+                                               s.krow8 ? s.krow8 + k * words : nullptr);
                 dom = dom || (__fmul_rn(alpha, dk) <= dist);
             }
             if (!__any_sync(kFull, dom)) {
@@ -343,6 +358,8 @@ __device__ void prune_and_store(const GraphBuildArgs& a, uint32_t u, uint32_t c,
                     s.kept_dist[kn] = dist;
                     s.kept_flag[i] = 1;
                 }
+                if (s.krow8)
+                    for (uint32_t w = lane; w < words; w += 32) s.krow8[kn * words + w] = s.crow8[w];
                 ++kn;
                 __syncwarp();
             }
@@ -376,6 +393,8 @@ __global__ void __launch_bounds__(32) k_gb_prune(const GraphBuildArgs a, unsigne
     s.kept_dist = reinterpret_cast<float*>(p);
     p += 64u * 4u;
     s.kept_flag = p;
+    p += (a.prune_cap + 15u) & ~15u;
+    s.krow8 = kept_row_cache_bytes(a) ? reinterpret_cast<uint32_t*>(p) : nullptr;
     unsigned err = 0;
     uint32_t segs = 0;
     if (JOB == kJobReverse) segs = a.ovf_pass ? *a.ovf_count : *a.seg_count;
@@ -509,7 +528,8 @@ PruneFn<JOB> select_prune(int dm) {
 }
 
 size_t prune_smem(const GraphBuildArgs& a) {
-    return static_cast<size_t>(a.prune_cap) * 9u + a.sp.row_stride * 4u + ((a.sp.row_bytes + 15u) & ~15u) + 512u;
+    return static_cast<size_t>(a.prune_cap) * 8u + ((a.prune_cap + 15u) & ~15u) + a.sp.row_stride * 4u +
+           ((a.sp.row_bytes + 15u) & ~15u) + 512u + kept_row_cache_bytes(a);
 }
 
 int dm_of(const GraphBuildArgs& a) {
