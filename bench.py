@@ -586,8 +586,9 @@ def run_ours(args, rank, world, local_rank):
             "frac_useful": round(achieved_useful / peak, 4),
         },
         "e2e": {"value": round(e2e_value, 1), "unit": "queries/s",
-                "h2d_bytes_per_step": int(nq * base.shape[1] * 4),
-                "d2h_bytes_per_step": int(nq * K * 8)},
+                # all ranks' queries and results (the job's step, like `value`)
+                "h2d_bytes_per_step": int(nq_job * base.shape[1] * 4),
+                "d2h_bytes_per_step": int(nq_job * K * 8)},
         "gpu_launches": args.steps,
         "clocks": clk.summary(),
     }
