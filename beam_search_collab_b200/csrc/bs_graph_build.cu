@@ -626,7 +626,16 @@ cudaError_t graph_build_batch(GraphBuildArgs& a, size_t smem_optin, int num_sms,
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     // 2. the targets' lists
-    if ((e = launch_prune<kJobTargets>(a, a.count, num_sms, stream)) != cudaSuccess) return e;
+    {
+        // a target's pool holds at most pool_cap expanded nodes: room for
+        // exactly that many candidates (smaller shared memory, more prunes
+        // per SM than the general 4,096)
+        GraphBuildArgs t = a;
+        uint32_t cap = 64;
+        while (cap < a.pool_cap) cap <<= 1;
+        if (cap < t.prune_cap) t.prune_cap = cap;
+        if ((e = launch_prune<kJobTargets>(t, a.count, num_sms, stream)) != cudaSuccess) return e;
+    }
     // 3. reverse edges, stably sorted by destination
     const uint64_t items = a.count * a.degree;
     const unsigned tb = static_cast<unsigned>(std::min<uint64_t>((items + 255) / 256, 65535ull * 8));
@@ -659,7 +668,12 @@ cudaError_t graph_build_batch(GraphBuildArgs& a, size_t smem_optin, int num_sms,
 
 cudaError_t graph_build_finish(GraphBuildArgs& a, size_t smem_optin, int num_sms, cudaStream_t stream) {
     (void)smem_optin;
-    return launch_prune<kJobFinish>(a, a.sp.n, num_sms, stream);
+    // a final list holds at most degree ids
+    GraphBuildArgs f = a;
+    uint32_t cap = 64;
+    while (cap < a.degree) cap <<= 1;
+    if (cap < f.prune_cap) f.prune_cap = cap;
+    return launch_prune<kJobFinish>(f, a.sp.n, num_sms, stream);
 }
 
 }  // namespace bsb
